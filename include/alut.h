@@ -1,0 +1,204 @@
+/*
+ * alut.h - C ABI of the B200 (sm_100a) approximate-lookup-table (ALUT) path of TableMoE.
+ *
+ * The ALUT path replaces a skipped routed expert's output by a cached one:
+ *   1. project the token's hidden state onto the layer's per-modality PCA basis,
+ *   2. find the centroid of the (expert, modality) key table with the largest inner
+ *      product (first index wins ties), with a hit threshold,
+ *   3. gather that centroid's cached expert output (the value row),
+ *   4. scale it by the renormalised routing weight and accumulate it into the layer output.
+ *
+ * Every entry point is asynchronous on the stream it is given, takes plain device
+ * pointers and sizes, and returns ALUT_OK (0) or a negative alut_status_t. Argument
+ * errors are detected on the host before anything is launched. Nothing here allocates
+ * device memory: scratch lives in a caller-owned workspace whose size comes from
+ * alut_workspace_size() and which must be zero-filled once before its first use (the
+ * kernels leave it reusable). Calls that share one workspace must be ordered on the
+ * GPU (same stream, or events between streams).
+ *
+ * Reference interfaces replaced (paths are inside the reference project
+ * fanyalun/tablemoe-sc26):
+ *   alut_project          table_moe/cache_engine/search.py:476  _project_queries_into
+ *   alut_search           table_moe/cache_engine/search.py:515  _search_prefill_offline_into
+ *                         table_moe/cache_engine/search.py:566  _search_decode_offline_from_low_into
+ *                         table_moe/cache_engine/search.py:604  _search_decode_offline_into
+ *                         table_moe/cache_engine/search.py:661  _search_offline_dot_from_low_into
+ *                         table_moe/cache_engine/search.py:715  search_decode_offline_dot
+ *   alut_gather_rows      table_moe/cache_engine/manager.py:212 gather_values
+ *                         table_moe/cache_engine/manager.py:216 gather_values_decode_bs1
+ *   alut_combine          table_moe/models/qwen3_vl_moe/cached_layers.py:455-465 (lookup slots)
+ *                         table_moe/models/deepseek_vl2/deepseek_layers.py:707-729
+ *                         table_moe/skip/pruning.py:55 renormalize_surviving_weights
+ *   alut_lookup_combine   search + combine in one call (no single reference counterpart;
+ *                         it chains search.py:808 and cached_layers.py:340-465)
+ *   alut_search_packed /
+ *   alut_merge_packed     centroid-range sharding of one large table (new: the reference
+ *                         is single-GPU; the merge rule is the tie rule of search.py:89)
+ */
+#ifndef ALUT_H_
+#define ALUT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* alut_stream_t; /* == cudaStream_t; NULL is the legacy default stream */
+
+typedef enum alut_dtype {
+  ALUT_F32 = 0,
+  ALUT_BF16 = 1,
+  ALUT_F16 = 2,
+} alut_dtype_t;
+
+typedef enum alut_status {
+  ALUT_OK = 0,
+  ALUT_EINVAL = -1,     /* null pointer, negative size, bad enum */
+  ALUT_EDTYPE = -2,     /* dtype combination not supported */
+  ALUT_ESHAPE = -3,     /* shape/stride not supported (e.g. non-unit innermost stride) */
+  ALUT_ECUDA = -4,      /* a CUDA launch or API call failed; see alut_last_error() */
+  ALUT_EWORKSPACE = -5, /* workspace missing or smaller than alut_workspace_size() */
+  ALUT_ERANGE = -6,     /* size beyond what the build supports */
+} alut_status_t;
+
+/* Which centroid table a search scores against (manager.py:44-53). */
+typedef enum alut_keyset {
+  ALUT_KEYS_NORMALISED = 0, /* keys_buffer: rows L2-normalised at load (cosine variants) */
+  ALUT_KEYS_RAW = 1,        /* raw_keys_buffer (dot variants) */
+} alut_keyset_t;
+
+/* How alut_combine rescales the routing weights of surviving slots
+ * (skip/pruning.py:55-73). A slot survives when it was computed (compute_mask) or when
+ * its lookup hit. */
+typedef enum alut_renorm {
+  ALUT_RENORM_NONE = 0,      /* weights are final as given */
+  ALUT_RENORM_TO_ONE = 1,    /* w*surv / sum(w*surv)               (Qwen3-VL wrapper) */
+  ALUT_RENORM_TO_ROWSUM = 2, /* w*surv / sum(w*surv) * sum(w)       (DeepSeek-VL2 wrapper) */
+} alut_renorm_t;
+
+/* One layer's tables, all device-resident. Modality 0 = vision, 1 = text
+ * (config.py:28). Strides are in elements; the innermost stride of every tensor is 1. */
+typedef struct alut_tables {
+  int32_t num_experts; /* E */
+  int32_t k;           /* K centroids per (expert, modality) */
+  int32_t l;           /* L, PCA rank */
+  int32_t h;           /* H, hidden size */
+  int32_t key_dtype;   /* alut_dtype_t of keys and raw_keys */
+  int32_t value_dtype; /* alut_dtype_t of values */
+  int32_t proj_dtype;  /* alut_dtype_t of proj and bias */
+  int32_t reserved0;
+  const void* keys;     /* [E,2,K,L] keys_buffer (may be NULL if only RAW is used) */
+  const void* raw_keys; /* [E,2,K,L] raw_keys_buffer (may be NULL if only NORMALISED is used) */
+  const void* values;   /* [E,2,K,H] values_buffer (may be NULL for search-only calls) */
+  const void* proj[2];  /* [H,L] per modality */
+  const void* bias[2];  /* [L] per modality (= -mean @ proj, manager.py:166) */
+  int64_t key_stride[3];   /* strides of dims e, m, k (keys and raw_keys share them) */
+  int64_t value_stride[3]; /* strides of dims e, m, k */
+  int64_t proj_stride_h;   /* row stride of proj */
+} alut_tables_t;
+
+/* One batch of routed tokens. */
+typedef struct alut_batch {
+  int32_t q;       /* tokens */
+  int32_t s;       /* routed slots per token (top_k) */
+  int32_t x_dtype; /* alut_dtype_t of x */
+  int32_t reserved0;
+  const void* x;            /* [Q,H] hidden states */
+  int64_t x_stride;         /* row stride of x */
+  const int64_t* sel;       /* [Q,S] selected expert ids */
+  int64_t sel_stride;       /* row stride of sel */
+  const uint8_t* is_vision; /* [Q] bool, nonzero = vision modality */
+  const uint8_t* reuse;     /* [Q,S] bool search mask; NULL = every slot searched */
+  int64_t reuse_stride;     /* row stride of reuse */
+} alut_batch_t;
+
+/* Search parameters (config.py:34-37). */
+typedef struct alut_search_params {
+  int32_t keyset;       /* alut_keyset_t */
+  int32_t normalize_q;  /* 1: L2-normalise the projected query (search.py:495, prefill cosine) */
+  int32_t cmp_ge;       /* 1: hit = max >= thr (search.py:597); 0: hit = max > thr (search.py:689) */
+  int32_t reserved0;
+  float thr_vision;     /* threshold for vision tokens */
+  float thr_text;       /* threshold for text tokens */
+  float eps;            /* OFFLINE_COSINE_EPS (search.py:13-18) */
+  float reserved1;
+} alut_search_params_t;
+
+/* Bytes of workspace needed for batches of up to q tokens x s slots on these tables.
+ * Returns 0 on invalid arguments. */
+size_t alut_workspace_size(const alut_tables_t* tables, int32_t q, int32_t s);
+
+/* a1: q_low[Q,L] = x[mask_m] @ proj_m + bias_m per modality, optionally L2-normalised,
+ * written in the key dtype (search.py:476-498). */
+int alut_project(const alut_tables_t* tables, const alut_batch_t* batch, int32_t normalize_q,
+                 float eps, void* q_low, int64_t q_low_stride, void* workspace,
+                 size_t workspace_bytes, alut_stream_t stream);
+
+/* a2-a5: for every slot with reuse: idx = argmax_k q_low . key[e,m,k] (first index on
+ * ties), hit = threshold rule. Slots without reuse, and misses, get hit=0, idx=0 (the
+ * reference's pre-zeroed outputs). out_hit/out_idx are [Q,S] with row stride out_stride.
+ * q_low_in may hold a precomputed [Q,L] query in the key dtype (row stride l); when NULL
+ * the query is projected from batch->x. */
+int alut_search(const alut_tables_t* tables, const alut_batch_t* batch,
+                const alut_search_params_t* params, const void* q_low_in, uint8_t* out_hit,
+                int64_t* out_idx, int64_t out_stride, void* workspace, size_t workspace_bytes,
+                alut_stream_t stream);
+
+/* a7: out[r_i,:] = values[eids[i], mids[i], cids[i], :] for i < n, a bit-exact copy
+ * (manager.py:212-213), with r_i = out_rows[i] when out_rows is given (the slot scatter of
+ * gather_values_decode_bs1, manager.py:216-228) and r_i = i otherwise. out has the value
+ * dtype and row stride out_stride. Out-of-range ids give a zero row. */
+int alut_gather_rows(const alut_tables_t* tables, int32_t n, const int64_t* eids,
+                     const int64_t* mids, const int64_t* cids, const int64_t* out_rows,
+                     void* out, int64_t out_stride, alut_stream_t stream);
+
+/* a8 for the lookup slots: for each token t,
+ *   out[t,:] = (accumulate ? out[t,:] : 0) + sum_{s: hit[t,s]} w~[t,s] * values[sel[t,s], m_t, idx[t,s], :]
+ * with w~ the renormalised weights of renorm (survivors = compute_mask | hit;
+ * compute_mask NULL means no computed slots). Arithmetic is fp32; out has out_dtype. */
+int alut_combine(const alut_tables_t* tables, const alut_batch_t* batch, const uint8_t* hit,
+                 const int64_t* idx, int64_t hit_stride, const float* weights,
+                 int64_t weight_stride, const uint8_t* compute_mask, int64_t compute_stride,
+                 int32_t renorm, int32_t accumulate, void* out, int64_t out_stride,
+                 int32_t out_dtype, alut_stream_t stream);
+
+/* alut_search followed by alut_combine without the hit/idx round trip through the
+ * caller. out_hit/out_idx may be NULL. */
+int alut_lookup_combine(const alut_tables_t* tables, const alut_batch_t* batch,
+                        const alut_search_params_t* params, const float* weights,
+                        int64_t weight_stride, const uint8_t* compute_mask,
+                        int64_t compute_stride, int32_t renorm, int32_t accumulate, void* out,
+                        int64_t out_stride, int32_t out_dtype, uint8_t* out_hit,
+                        int64_t* out_idx, int64_t out_stride_hit, void* workspace,
+                        size_t workspace_bytes, alut_stream_t stream);
+
+/* Centroid-range shard: search a table slice whose row 0 is global centroid idx_offset
+ * and write, per (token, slot), the packed best candidate
+ *   (order-preserving bits of the score << 32) | (0xFFFFFFFF - global index)
+ * so that the largest packed value is the best score with the lowest index; 0 means no
+ * candidate. out_packed is [Q*S] (row-major). */
+int alut_search_packed(const alut_tables_t* tables, const alut_batch_t* batch,
+                       const alut_search_params_t* params, const void* q_low_in,
+                       int64_t idx_offset, uint64_t* out_packed, void* workspace,
+                       size_t workspace_bytes, alut_stream_t stream);
+
+/* Merge `world` packed candidate arrays ([world][n], contiguous) by max and apply the
+ * threshold rule of params to give hit/idx for n = Q*S slots (row-major, no gaps).
+ * is_vision may be NULL (all text). Slots whose candidates are all 0 miss. */
+int alut_merge_packed(int32_t world, int32_t q, int32_t s, const uint64_t* packed_all,
+                      const uint8_t* is_vision, const alut_search_params_t* params,
+                      uint8_t* out_hit, int64_t* out_idx, alut_stream_t stream);
+
+/* Text of the last error seen by this thread (never NULL). */
+const char* alut_last_error(void);
+
+/* Library version, as major*10000 + minor*100 + patch. */
+int alut_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ALUT_H_ */

@@ -1,0 +1,565 @@
+// C ABI of the ALUT path (declared in include/alut.h): argument checks on the host,
+// dtype dispatch, and the launch sequence project+plan -> search -> finalize/combine.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "alut_combine.cuh"
+#include "alut_common.cuh"
+#include "alut_project.cuh"
+#include "alut_search.cuh"
+
+namespace alut {
+
+static thread_local char g_err[512] = "no error";
+
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  return ALUT_OK;
+}
+
+float host_round_as(float v, int dtype) {
+  if (dtype == ALUT_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dtype == ALUT_F16) return __half2float(__float2half_rn(v));
+  return v;
+}
+
+static int dtype_size(int d) { return d == ALUT_F32 ? 4 : 2; }
+static bool dtype_ok(int d) { return d == ALUT_F32 || d == ALUT_BF16 || d == ALUT_F16; }
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+  if (dev < 64 && cache[dev]) return cache[dev];
+  int n = 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 148;
+  if (dev < 64) cache[dev] = n;
+  return n;
+}
+
+// Raise a kernel's dynamic shared memory limit once per (kernel, device).
+static int allow_smem(const void* kernel, size_t bytes) {
+  if (bytes <= 48 * 1024) return ALUT_OK;
+  struct Entry { const void* k; int dev; int bytes; };
+  static Entry table[256];
+  static int used = 0;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (table[i].k == kernel && table[i].dev == dev && table[i].bytes >= static_cast<int>(bytes))
+      return ALUT_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(bytes));
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (used < 256) table[used++] = Entry{kernel, dev, static_cast<int>(bytes)};
+  return ALUT_OK;
+}
+
+static int check_tables(const alut_tables_t* t, bool need_proj) {
+  if (!t) return fail(ALUT_EINVAL, "tables is NULL");
+  if (t->num_experts <= 0 || t->k <= 0 || t->l <= 0 || t->h <= 0)
+    return fail(ALUT_EINVAL, "tables: num_experts=%d k=%d l=%d h=%d must be positive",
+                t->num_experts, t->k, t->l, t->h);
+  if (2 * static_cast<int64_t>(t->num_experts) > kMaxTables)
+    return fail(ALUT_ERANGE, "tables: num_experts=%d exceeds %d", t->num_experts, kMaxTables / 2);
+  if (t->l > kMaxL) return fail(ALUT_ERANGE, "tables: l=%d exceeds %d", t->l, kMaxL);
+  if (!dtype_ok(t->key_dtype) || !dtype_ok(t->value_dtype) || !dtype_ok(t->proj_dtype))
+    return fail(ALUT_EDTYPE, "tables: unknown dtype");
+  if (need_proj) {
+    if (t->proj_dtype != t->key_dtype)
+      return fail(ALUT_EDTYPE, "tables: proj dtype (%d) must equal key dtype (%d)", t->proj_dtype,
+                  t->key_dtype);
+    for (int m = 0; m < 2; ++m)
+      if (!t->proj[m] || !t->bias[m]) return fail(ALUT_EINVAL, "tables: proj/bias[%d] is NULL", m);
+    if (t->proj_stride_h < t->l) return fail(ALUT_ESHAPE, "tables: proj_stride_h < l");
+  }
+  return ALUT_OK;
+}
+
+static int check_batch(const alut_tables_t* t, const alut_batch_t* b, bool need_x) {
+  if (!b) return fail(ALUT_EINVAL, "batch is NULL");
+  if (b->q < 0 || b->s < 0) return fail(ALUT_EINVAL, "batch: q=%d s=%d", b->q, b->s);
+  if (b->s > kMaxSlots) return fail(ALUT_ERANGE, "batch: s=%d exceeds %d", b->s, kMaxSlots);
+  if (static_cast<int64_t>(b->q) * b->s >= (1ll << 31))
+    return fail(ALUT_ERANGE, "batch: q*s too large");
+  if (b->q == 0 || b->s == 0) return ALUT_OK;
+  if (!b->sel || !b->is_vision) return fail(ALUT_EINVAL, "batch: sel/is_vision is NULL");
+  if (b->sel_stride < b->s) return fail(ALUT_ESHAPE, "batch: sel_stride < s");
+  if (b->reuse && b->reuse_stride < b->s) return fail(ALUT_ESHAPE, "batch: reuse_stride < s");
+  if (need_x) {
+    if (!b->x) return fail(ALUT_EINVAL, "batch: x is NULL");
+    if (!dtype_ok(b->x_dtype)) return fail(ALUT_EDTYPE, "batch: unknown x dtype");
+    if (b->x_stride < t->h) return fail(ALUT_ESHAPE, "batch: x_stride < h");
+  }
+  return ALUT_OK;
+}
+
+static int check_params(const alut_tables_t* t, const alut_search_params_t* p, const void** keys) {
+  if (!p) return fail(ALUT_EINVAL, "params is NULL");
+  if (p->keyset == ALUT_KEYS_NORMALISED) *keys = t->keys;
+  else if (p->keyset == ALUT_KEYS_RAW) *keys = t->raw_keys;
+  else return fail(ALUT_EINVAL, "params: bad keyset %d", p->keyset);
+  if (!*keys) return fail(ALUT_EINVAL, "tables: key set %d is NULL", p->keyset);
+  if (t->key_stride[2] < t->l)
+    return fail(ALUT_ESHAPE, "tables: key_stride_k < l");
+  return ALUT_OK;
+}
+
+// ---- launches ------------------------------------------------------------------------
+
+template <typename TX, typename TK>
+static int launch_project_plan_t(const ProjPlanArgs& a, int grid, size_t smem, cudaStream_t st) {
+  auto kern = k_project_plan<TX, TK, TK>;
+  int rc = allow_smem(reinterpret_cast<const void*>(kern), smem);
+  if (rc) return rc;
+  kern<<<grid, kProjThreads, smem, st>>>(a);
+  return check_launch("k_project_plan");
+}
+
+template <typename TK>
+static int launch_project_plan_k(int x_dtype, const ProjPlanArgs& a, int grid, size_t smem,
+                                 cudaStream_t st) {
+  switch (x_dtype) {
+    case ALUT_F32: return launch_project_plan_t<float, TK>(a, grid, smem, st);
+    case ALUT_BF16: return launch_project_plan_t<__nv_bfloat16, TK>(a, grid, smem, st);
+    case ALUT_F16: return launch_project_plan_t<__half, TK>(a, grid, smem, st);
+  }
+  return fail(ALUT_EDTYPE, "x dtype");
+}
+
+static int launch_project_plan(int key_dtype, int x_dtype, const ProjPlanArgs& a, int grid,
+                               size_t smem, cudaStream_t st) {
+  switch (key_dtype) {
+    case ALUT_F32: return launch_project_plan_k<float>(x_dtype, a, grid, smem, st);
+    case ALUT_BF16: return launch_project_plan_k<__nv_bfloat16>(x_dtype, a, grid, smem, st);
+    case ALUT_F16: return launch_project_plan_k<__half>(x_dtype, a, grid, smem, st);
+  }
+  return fail(ALUT_EDTYPE, "key dtype");
+}
+
+template <typename TK>
+static int launch_search_t(bool vec, const SearchArgs& a, int grid, size_t smem, cudaStream_t st) {
+  if (vec) {
+    int rc = allow_smem(reinterpret_cast<const void*>(k_search<TK, true>), smem);
+    if (rc) return rc;
+    k_search<TK, true><<<grid, kSearchThreads, smem, st>>>(a);
+  } else {
+    int rc = allow_smem(reinterpret_cast<const void*>(k_search<TK, false>), smem);
+    if (rc) return rc;
+    k_search<TK, false><<<grid, kSearchThreads, smem, st>>>(a);
+  }
+  return check_launch("k_search");
+}
+
+static int launch_search(int key_dtype, bool vec, const SearchArgs& a, int grid, size_t smem,
+                         cudaStream_t st) {
+  switch (key_dtype) {
+    case ALUT_F32: return launch_search_t<float>(vec, a, grid, smem, st);
+    case ALUT_BF16: return launch_search_t<__nv_bfloat16>(vec, a, grid, smem, st);
+    case ALUT_F16: return launch_search_t<__half>(vec, a, grid, smem, st);
+  }
+  return fail(ALUT_EDTYPE, "key dtype");
+}
+
+template <typename TV, typename TO>
+static int launch_combine_t(bool vec, const CombineArgs& a, dim3 grid, cudaStream_t st) {
+  if (vec) k_combine<TV, TO, true><<<grid, kCombineThreads, 0, st>>>(a);
+  else k_combine<TV, TO, false><<<grid, kCombineThreads, 0, st>>>(a);
+  return check_launch("k_combine");
+}
+
+static int launch_combine(int vd, int od, bool vec, const CombineArgs& a, dim3 grid,
+                          cudaStream_t st) {
+  if (vd == ALUT_BF16 && od == ALUT_BF16) return launch_combine_t<__nv_bfloat16, __nv_bfloat16>(vec, a, grid, st);
+  if (vd == ALUT_F16 && od == ALUT_F16) return launch_combine_t<__half, __half>(vec, a, grid, st);
+  if (vd == ALUT_F32 && od == ALUT_F32) return launch_combine_t<float, float>(vec, a, grid, st);
+  if (vd == ALUT_BF16 && od == ALUT_F32) return launch_combine_t<__nv_bfloat16, float>(vec, a, grid, st);
+  if (vd == ALUT_F16 && od == ALUT_F32) return launch_combine_t<__half, float>(vec, a, grid, st);
+  return fail(ALUT_EDTYPE, "combine: value dtype %d with out dtype %d not supported", vd, od);
+}
+
+// Projection + plan + centroid scan into the packed best buffer `best`.
+static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_search_params_t* p,
+                      const void* keys, const void* q_low_in, uint32_t idx_offset,
+                      uint64_t* best, void* workspace, size_t ws_bytes, cudaStream_t st) {
+  const Workspace w = workspace_layout(b->q, b->s, t->l, 2 * t->num_experts);
+  if (!workspace) return fail(ALUT_EWORKSPACE, "workspace is NULL");
+  if (ws_bytes < w.total)
+    return fail(ALUT_EWORKSPACE, "workspace has %zu bytes, needs %zu", ws_bytes, w.total);
+  if (!aligned16(workspace)) return fail(ALUT_EWORKSPACE, "workspace must be 16-byte aligned");
+  char* base = static_cast<char*>(workspace);
+
+  ProjPlanArgs a{};
+  a.x = b->x;
+  a.x_stride = b->x_stride;
+  a.is_vision = b->is_vision;
+  for (int m = 0; m < 2; ++m) {
+    a.proj[m] = t->proj[m];
+    a.bias[m] = t->bias[m];
+  }
+  a.proj_stride = t->proj_stride_h;
+  a.q_in = q_low_in;
+  a.q = b->q;
+  a.h = t->h;
+  a.l = t->l;
+  a.qtiles = ceil_div(b->q, kProjTileQ);
+  a.nsplit = q_low_in ? 1 : proj_splits(b->q, t->h);
+  a.normalize = p->normalize_q;
+  a.eps = p->eps;
+  a.qpart = reinterpret_cast<float*>(base + w.qpart);
+  a.qlow = reinterpret_cast<float*>(base + w.qlow);
+  a.counters = reinterpret_cast<uint32_t*>(base + w.counters);
+  a.do_plan = 1;
+  a.s = b->s;
+  a.num_experts = t->num_experts;
+  a.sel = b->sel;
+  a.sel_stride = b->sel_stride;
+  a.reuse = b->reuse;
+  a.reuse_stride = b->reuse_stride;
+  a.best = best;
+  a.sorted = reinterpret_cast<int*>(base + w.sorted);
+  a.groups = reinterpret_cast<int4*>(base + w.groups);
+  a.meta = reinterpret_cast<int*>(base + w.meta);
+  const size_t smem1 = std::max(proj_smem_bytes(t->l), plan_smem_bytes(2 * t->num_experts));
+  int rc = launch_project_plan(t->key_dtype, b->x_dtype, a, a.qtiles * a.nsplit + 1, smem1, st);
+  if (rc) return rc;
+
+  SearchArgs s{};
+  s.keys = keys;
+  s.key_stride_e = t->key_stride[0];
+  s.key_stride_m = t->key_stride[1];
+  s.key_stride_k = t->key_stride[2];
+  s.k = t->k;
+  s.l = t->l;
+  s.s = b->s;
+  s.nchunks = ceil_div(t->k, kSearchChunkK);
+  s.idx_offset = idx_offset;
+  s.qlow = a.qlow;
+  s.sorted = a.sorted;
+  s.groups = a.groups;
+  s.meta = a.meta;
+  s.best = best;
+  const int esz = dtype_size(t->key_dtype);
+  const bool vec = (t->l % 8 == 0) && aligned16(keys) && (t->key_stride[0] * esz) % 16 == 0 &&
+                   (t->key_stride[1] * esz) % 16 == 0 && (t->key_stride[2] * esz) % 16 == 0;
+  const int64_t max_tiles = w.max_groups * s.nchunks;
+  const int grid = static_cast<int>(std::min<int64_t>(max_tiles, static_cast<int64_t>(num_sms()) * 8));
+  return launch_search(t->key_dtype, vec, s, std::max(grid, 1), search_smem_bytes(t->l), st);
+}
+
+static void fill_value_strides(const alut_tables_t* t, CombineArgs& c) {
+  c.values = t->values;
+  c.vs_e = t->value_stride[0];
+  c.vs_m = t->value_stride[1];
+  c.vs_k = t->value_stride[2];
+  c.h = t->h;
+  c.num_experts = t->num_experts;
+  c.k = t->k;
+}
+
+static bool combine_vec(const alut_tables_t* t, const void* out, int64_t out_stride, int od) {
+  const int vsz = dtype_size(t->value_dtype), osz = dtype_size(od);
+  return t->h % 8 == 0 && aligned16(t->values) && aligned16(out) &&
+         (t->value_stride[0] * vsz) % 16 == 0 && (t->value_stride[1] * vsz) % 16 == 0 &&
+         (t->value_stride[2] * vsz) % 16 == 0 && (out_stride * osz) % 16 == 0;
+}
+
+}  // namespace alut
+
+using namespace alut;
+
+extern "C" {
+
+int alut_version(void) { return 100; }
+
+const char* alut_last_error(void) { return g_err; }
+
+size_t alut_workspace_size(const alut_tables_t* tables, int32_t q, int32_t s) {
+  if (!tables || q < 0 || s < 0 || tables->l <= 0 || tables->num_experts <= 0) return 0;
+  return workspace_layout(q, s, tables->l, 2 * tables->num_experts).total;
+}
+
+int alut_project(const alut_tables_t* tables, const alut_batch_t* batch, int32_t normalize_q,
+                 float eps, void* q_low, int64_t q_low_stride, void* workspace,
+                 size_t workspace_bytes, alut_stream_t stream) {
+  int rc = check_tables(tables, true);
+  if (rc) return rc;
+  if (!batch) return fail(ALUT_EINVAL, "batch is NULL");
+  if (batch->q < 0) return fail(ALUT_EINVAL, "batch: q=%d", batch->q);
+  if (batch->q == 0) return ALUT_OK;
+  if (!batch->x || !batch->is_vision) return fail(ALUT_EINVAL, "batch: x/is_vision is NULL");
+  if (!dtype_ok(batch->x_dtype)) return fail(ALUT_EDTYPE, "batch: unknown x dtype");
+  if (batch->x_stride < tables->h) return fail(ALUT_ESHAPE, "batch: x_stride < h");
+  if (!q_low || q_low_stride < tables->l) return fail(ALUT_EINVAL, "q_low is NULL or stride < l");
+  const Workspace w = workspace_layout(batch->q, 0, tables->l, 2 * tables->num_experts);
+  if (!workspace || workspace_bytes < w.total)
+    return fail(ALUT_EWORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, w.total);
+  char* base = static_cast<char*>(workspace);
+  ProjPlanArgs a{};
+  a.x = batch->x;
+  a.x_stride = batch->x_stride;
+  a.is_vision = batch->is_vision;
+  for (int m = 0; m < 2; ++m) {
+    a.proj[m] = tables->proj[m];
+    a.bias[m] = tables->bias[m];
+  }
+  a.proj_stride = tables->proj_stride_h;
+  a.q = batch->q;
+  a.h = tables->h;
+  a.l = tables->l;
+  a.qtiles = ceil_div(batch->q, kProjTileQ);
+  a.nsplit = proj_splits(batch->q, tables->h);
+  a.normalize = normalize_q;
+  a.eps = eps;
+  a.qpart = reinterpret_cast<float*>(base + w.qpart);
+  a.qlow = reinterpret_cast<float*>(base + w.qlow);
+  a.counters = reinterpret_cast<uint32_t*>(base + w.counters);
+  a.q_out = q_low;
+  a.q_out_stride = q_low_stride;
+  a.do_plan = 0;
+  return launch_project_plan(tables->key_dtype, batch->x_dtype, a, a.qtiles * a.nsplit,
+                             proj_smem_bytes(tables->l), reinterpret_cast<cudaStream_t>(stream));
+}
+
+int alut_search(const alut_tables_t* tables, const alut_batch_t* batch,
+                const alut_search_params_t* params, const void* q_low_in, uint8_t* out_hit,
+                int64_t* out_idx, int64_t out_stride, void* workspace, size_t workspace_bytes,
+                alut_stream_t stream) {
+  int rc = check_tables(tables, q_low_in == nullptr);
+  if (rc) return rc;
+  rc = check_batch(tables, batch, q_low_in == nullptr);
+  if (rc) return rc;
+  const void* keys = nullptr;
+  rc = check_params(tables, params, &keys);
+  if (rc) return rc;
+  if (batch->q == 0 || batch->s == 0) return ALUT_OK;
+  if (!out_hit || !out_idx) return fail(ALUT_EINVAL, "out_hit/out_idx is NULL");
+  if (out_stride < batch->s) return fail(ALUT_ESHAPE, "out_stride < s");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const Workspace w = workspace_layout(batch->q, batch->s, tables->l, 2 * tables->num_experts);
+  if (!workspace || workspace_bytes < w.total)
+    return fail(ALUT_EWORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, w.total);
+  uint64_t* best = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + w.best);
+  rc = run_search(tables, batch, params, keys, q_low_in, 0u, best, workspace, workspace_bytes, st);
+  if (rc) return rc;
+  FinalizeArgs f{};
+  f.best = best;
+  f.sel = batch->sel;
+  f.sel_stride = batch->sel_stride;
+  f.is_vision = batch->is_vision;
+  f.reuse = batch->reuse;
+  f.reuse_stride = batch->reuse_stride;
+  f.q = batch->q;
+  f.s = batch->s;
+  f.num_experts = tables->num_experts;
+  f.cmp_ge = params->cmp_ge;
+  f.thr_vis = host_round_as(params->thr_vision, tables->key_dtype);
+  f.thr_txt = host_round_as(params->thr_text, tables->key_dtype);
+  f.out_hit = out_hit;
+  f.out_idx = out_idx;
+  f.out_stride = out_stride;
+  const int64_t n = static_cast<int64_t>(batch->q) * batch->s;
+  k_finalize<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(f);
+  return check_launch("k_finalize");
+}
+
+int alut_gather_rows(const alut_tables_t* tables, int32_t n, const int64_t* eids,
+                     const int64_t* mids, const int64_t* cids, const int64_t* out_rows,
+                     void* out, int64_t out_stride, alut_stream_t stream) {
+  if (!tables) return fail(ALUT_EINVAL, "tables is NULL");
+  if (n < 0) return fail(ALUT_EINVAL, "n=%d", n);
+  if (n == 0) return ALUT_OK;
+  if (!tables->values || !eids || !mids || !cids || !out)
+    return fail(ALUT_EINVAL, "values/eids/mids/cids/out is NULL");
+  if (!dtype_ok(tables->value_dtype)) return fail(ALUT_EDTYPE, "value dtype");
+  if (tables->h <= 0 || tables->k <= 0 || tables->num_experts <= 0)
+    return fail(ALUT_EINVAL, "tables: bad sizes");
+  if (out_stride < tables->h) return fail(ALUT_ESHAPE, "out_stride < h");
+  const int esz = dtype_size(tables->value_dtype);
+  GatherArgs g{};
+  g.values = static_cast<const char*>(tables->values);
+  g.vs_e = tables->value_stride[0] * esz;
+  g.vs_m = tables->value_stride[1] * esz;
+  g.vs_k = tables->value_stride[2] * esz;
+  g.row_bytes = static_cast<int64_t>(tables->h) * esz;
+  g.esz = esz;
+  g.num_experts = tables->num_experts;
+  g.k = tables->k;
+  g.eids = eids;
+  g.mids = mids;
+  g.cids = cids;
+  g.out_rows = out_rows;
+  g.out = static_cast<char*>(out);
+  g.out_stride = out_stride * esz;
+  g.vec = aligned16(tables->values) && aligned16(out) && g.vs_e % 16 == 0 && g.vs_m % 16 == 0 &&
+          g.vs_k % 16 == 0 && g.row_bytes % 16 == 0 && g.out_stride % 16 == 0;
+  const int64_t words = g.vec ? g.row_bytes / 16 : g.row_bytes;
+  const int ychunks = static_cast<int>(std::min<int64_t>(std::max<int64_t>((words + 127) / 128, 1), 64));
+  k_gather_rows<<<dim3(n, ychunks), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(g);
+  return check_launch("k_gather_rows");
+}
+
+int alut_combine(const alut_tables_t* tables, const alut_batch_t* batch, const uint8_t* hit,
+                 const int64_t* idx, int64_t hit_stride, const float* weights,
+                 int64_t weight_stride, const uint8_t* compute_mask, int64_t compute_stride,
+                 int32_t renorm, int32_t accumulate, void* out, int64_t out_stride,
+                 int32_t out_dtype, alut_stream_t stream) {
+  if (!tables) return fail(ALUT_EINVAL, "tables is NULL");
+  if (!tables->values) return fail(ALUT_EINVAL, "tables: values is NULL");
+  if (tables->num_experts <= 0 || tables->k <= 0 || tables->h <= 0)
+    return fail(ALUT_EINVAL, "tables: bad sizes");
+  int rc = check_batch(tables, batch, false);
+  if (rc) return rc;
+  if (batch->q == 0) return ALUT_OK;
+  if (!out || out_stride < tables->h) return fail(ALUT_EINVAL, "out is NULL or stride < h");
+  if (batch->s > 0 && (!hit || !idx || !weights)) return fail(ALUT_EINVAL, "hit/idx/weights is NULL");
+  if (batch->s > 0 && (hit_stride < batch->s || weight_stride < batch->s))
+    return fail(ALUT_ESHAPE, "hit_stride/weight_stride < s");
+  if (compute_mask && compute_stride < batch->s) return fail(ALUT_ESHAPE, "compute_stride < s");
+  if (renorm < ALUT_RENORM_NONE || renorm > ALUT_RENORM_TO_ROWSUM)
+    return fail(ALUT_EINVAL, "bad renorm %d", renorm);
+  if (!dtype_ok(out_dtype)) return fail(ALUT_EDTYPE, "out dtype");
+  CombineArgs c{};
+  fill_value_strides(tables, c);
+  c.q = batch->q;
+  c.s = batch->s;
+  c.sel = batch->sel;
+  c.sel_stride = batch->sel_stride;
+  c.is_vision = batch->is_vision;
+  c.reuse = batch->reuse;
+  c.reuse_stride = batch->reuse_stride;
+  c.hit_in = hit;
+  c.idx_in = idx;
+  c.hit_stride = hit_stride;
+  c.w = weights;
+  c.w_stride = weight_stride;
+  c.compute = compute_mask;
+  c.compute_stride = compute_stride;
+  c.renorm = renorm;
+  c.accumulate = accumulate;
+  c.out = out;
+  c.out_stride = out_stride;
+  dim3 grid(batch->q, ceil_div(tables->h, kCombineSpan));
+  return launch_combine(tables->value_dtype, out_dtype, combine_vec(tables, out, out_stride, out_dtype),
+                        c, grid, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int alut_lookup_combine(const alut_tables_t* tables, const alut_batch_t* batch,
+                        const alut_search_params_t* params, const float* weights,
+                        int64_t weight_stride, const uint8_t* compute_mask,
+                        int64_t compute_stride, int32_t renorm, int32_t accumulate, void* out,
+                        int64_t out_stride, int32_t out_dtype, uint8_t* out_hit,
+                        int64_t* out_idx, int64_t out_stride_hit, void* workspace,
+                        size_t workspace_bytes, alut_stream_t stream) {
+  int rc = check_tables(tables, true);
+  if (rc) return rc;
+  if (!tables->values) return fail(ALUT_EINVAL, "tables: values is NULL");
+  rc = check_batch(tables, batch, true);
+  if (rc) return rc;
+  const void* keys = nullptr;
+  rc = check_params(tables, params, &keys);
+  if (rc) return rc;
+  if (batch->q == 0 || batch->s == 0) return ALUT_OK;
+  if (!out || out_stride < tables->h) return fail(ALUT_EINVAL, "out is NULL or stride < h");
+  if (!weights || weight_stride < batch->s) return fail(ALUT_EINVAL, "weights NULL or stride < s");
+  if (compute_mask && compute_stride < batch->s) return fail(ALUT_ESHAPE, "compute_stride < s");
+  if ((out_hit == nullptr) != (out_idx == nullptr)) return fail(ALUT_EINVAL, "out_hit and out_idx go together");
+  if (out_hit && out_stride_hit < batch->s) return fail(ALUT_ESHAPE, "out_stride_hit < s");
+  if (renorm < ALUT_RENORM_NONE || renorm > ALUT_RENORM_TO_ROWSUM)
+    return fail(ALUT_EINVAL, "bad renorm %d", renorm);
+  if (!dtype_ok(out_dtype)) return fail(ALUT_EDTYPE, "out dtype");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const Workspace w = workspace_layout(batch->q, batch->s, tables->l, 2 * tables->num_experts);
+  if (!workspace || workspace_bytes < w.total)
+    return fail(ALUT_EWORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, w.total);
+  uint64_t* best = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + w.best);
+  rc = run_search(tables, batch, params, keys, nullptr, 0u, best, workspace, workspace_bytes, st);
+  if (rc) return rc;
+  CombineArgs c{};
+  fill_value_strides(tables, c);
+  c.q = batch->q;
+  c.s = batch->s;
+  c.sel = batch->sel;
+  c.sel_stride = batch->sel_stride;
+  c.is_vision = batch->is_vision;
+  c.reuse = batch->reuse;
+  c.reuse_stride = batch->reuse_stride;
+  c.best = best;
+  c.cmp_ge = params->cmp_ge;
+  c.thr_vis = host_round_as(params->thr_vision, tables->key_dtype);
+  c.thr_txt = host_round_as(params->thr_text, tables->key_dtype);
+  c.w = weights;
+  c.w_stride = weight_stride;
+  c.compute = compute_mask;
+  c.compute_stride = compute_stride;
+  c.renorm = renorm;
+  c.accumulate = accumulate;
+  c.out = out;
+  c.out_stride = out_stride;
+  c.out_hit = out_hit;
+  c.out_idx = out_idx;
+  c.out_hit_stride = out_stride_hit;
+  dim3 grid(batch->q, ceil_div(tables->h, kCombineSpan));
+  return launch_combine(tables->value_dtype, out_dtype, combine_vec(tables, out, out_stride, out_dtype),
+                        c, grid, st);
+}
+
+int alut_search_packed(const alut_tables_t* tables, const alut_batch_t* batch,
+                       const alut_search_params_t* params, const void* q_low_in,
+                       int64_t idx_offset, uint64_t* out_packed, void* workspace,
+                       size_t workspace_bytes, alut_stream_t stream) {
+  int rc = check_tables(tables, q_low_in == nullptr);
+  if (rc) return rc;
+  rc = check_batch(tables, batch, q_low_in == nullptr);
+  if (rc) return rc;
+  const void* keys = nullptr;
+  rc = check_params(tables, params, &keys);
+  if (rc) return rc;
+  if (batch->q == 0 || batch->s == 0) return ALUT_OK;
+  if (!out_packed) return fail(ALUT_EINVAL, "out_packed is NULL");
+  if (idx_offset < 0 || idx_offset + tables->k > 0xFFFFFFFFll)
+    return fail(ALUT_ERANGE, "idx_offset out of range");
+  return run_search(tables, batch, params, keys, q_low_in, static_cast<uint32_t>(idx_offset),
+                    out_packed, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int alut_merge_packed(int32_t world, int32_t q, int32_t s, const uint64_t* packed_all,
+                      const uint8_t* is_vision, const alut_search_params_t* params,
+                      uint8_t* out_hit, int64_t* out_idx, alut_stream_t stream) {
+  if (world <= 0 || q < 0 || s < 0) return fail(ALUT_EINVAL, "world=%d q=%d s=%d", world, q, s);
+  if (!params) return fail(ALUT_EINVAL, "params is NULL");
+  const int64_t n = static_cast<int64_t>(q) * s;
+  if (n == 0) return ALUT_OK;
+  if (!packed_all || !out_hit || !out_idx) return fail(ALUT_EINVAL, "packed_all/out is NULL");
+  MergeArgs m{};
+  m.packed = packed_all;
+  m.world = world;
+  m.n = n;
+  m.s = s;
+  m.is_vision = is_vision;
+  m.cmp_ge = params->cmp_ge;
+  m.thr_vis = params->thr_vision;
+  m.thr_txt = params->thr_text;
+  m.out_hit = out_hit;
+  m.out_idx = out_idx;
+  k_merge<<<static_cast<unsigned>((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(m);
+  return check_launch("k_merge");
+}
+
+}  // extern "C"

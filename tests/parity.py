@@ -1,0 +1,111 @@
+"""Fixture loading and the parity rules of the ALUT path, shared by the CPU and GPU tests.
+
+Parity rules (stated with the tolerances used):
+  * indices: bit-exact, except a slot whose top-2 fp64 score gap is below 1e-5 relative
+    (fp32 tables) - there the chosen centroid's exact score must lie within 1e-5 relative
+    of the best. For 16-bit tables the scores are compared after rounding to the table
+    dtype (the reference's bmm output dtype), so a slot may differ where the two
+    candidates' exact scores are within 2 ulp of that dtype.
+  * hit masks: equal, except where the best score lies within the same tolerance of the
+    threshold.
+  * gathered rows: bit-exact.
+  * combined output: |got - ref| <= 1e-2 * |ref| + 1e-2 * max|ref| (bf16 output).
+"""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+
+import oracle.oracle as orc
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+IDX_REL_TOL = 1e-5
+COMBINE_RTOL = 1e-2
+ULP = {"float32": 2.0 ** -23, "bfloat16": 2.0 ** -8, "float16": 2.0 ** -11}
+
+
+def golden_names():
+    return sorted(p.stem for p in GOLDEN.glob("*.npz"))
+
+
+def load_golden(name):
+    z = np.load(GOLDEN / f"{name}.npz")
+    meta = json.loads(str(z["meta"]))
+    d = {k: z[k] for k in z.files if k != "meta"}
+    d["x"] = orc.bf16_to_f32(d["x_bf16"]).reshape(d["x_bf16"].shape)
+    d["combined"] = orc.bf16_to_f32(d["combined_bf16"]).reshape(d["combined_bf16"].shape)
+    d["values_f32"] = orc.bf16_to_f32(d["values_bf16"]).reshape(d["values_bf16"].shape)
+    return meta, d
+
+
+def variant_rule(variant):
+    """(normalize query, key set, cmp_ge, thresholds source) of a reference entry point.
+
+    search.py:808 search_prefill_offline: normalised query, keys_buffer, >= (0.6, 0.7)
+    search.py:699 search_prefill_offline_dot: raw query, raw_keys_buffer, > OFFLINE_DOT_THRESHOLD
+    search.py:715 search_decode_offline_dot: same as prefill_dot
+    search.py:824 search_decode_offline (torch path): raw query, keys_buffer, >= 0
+    search.py:839 search_decode_hybrid (no online window): raw query, keys_buffer, >= 0
+    """
+    if variant == "prefill_cos":
+        return dict(normalize=True, keyset="norm", cmp_ge=True, thr=(0.6, 0.7))
+    if variant in ("prefill_dot", "decode_dot"):
+        return dict(normalize=False, keyset="raw", cmp_ge=False, thr=None)
+    if variant in ("decode_cos", "decode_hybrid"):
+        return dict(normalize=False, keyset="norm", cmp_ge=True, thr=(0.0, 0.0))
+    raise ValueError(variant)
+
+
+def case_inputs(meta, d):
+    """Everything the oracle needs for a golden case."""
+    rule = variant_rule(meta["variant"])
+    thr = rule["thr"] if rule["thr"] is not None else (meta.get("dot_thr", 0.0),) * 2
+    keys = d["keys_raw"] if rule["keyset"] == "raw" else d["keys_norm"]
+    return rule, thr, keys
+
+
+def check_search(got_hit, got_idx, ref_hit, ref_idx, q_low, keys, sel, is_vision, thr, dtype,
+                 what=""):
+    """Assert the index / hit parity rules; returns the number of exempted slots."""
+    got_hit = np.asarray(got_hit).astype(bool)
+    ref_hit = np.asarray(ref_hit).astype(bool)
+    got_idx = np.asarray(got_idx)
+    ref_idx = np.asarray(ref_idx)
+    is_vision = np.asarray(is_vision).astype(bool)
+    ulp = ULP[dtype]
+    exempt = 0
+    bad = []
+    for t, s in zip(*np.nonzero((got_hit != ref_hit) | (got_hit & (got_idx != ref_idx)))):
+        s_ref = orc.score(q_low, keys, sel, is_vision, t, s, int(ref_idx[t, s]))
+        th = thr[0] if is_vision[t] else thr[1]
+        if got_hit[t, s] != ref_hit[t, s]:
+            # Only the hit differs: the best score must sit on the threshold.
+            best = s_ref if ref_hit[t, s] else orc.score(q_low, keys, sel, is_vision, t, s, int(got_idx[t, s]))
+            tol = max(IDX_REL_TOL, 2 * ulp) * max(abs(th), abs(best), 1e-30)
+            if abs(best - th) <= tol:
+                exempt += 1
+                continue
+            bad.append((t, s, "hit", bool(got_hit[t, s]), bool(ref_hit[t, s]), best, th))
+            continue
+        s_got = orc.score(q_low, keys, sel, is_vision, t, s, int(got_idx[t, s]))
+        tol = (IDX_REL_TOL if dtype == "float32" else 2 * ulp) * max(abs(s_ref), abs(s_got), 1e-30)
+        if abs(s_ref - s_got) <= tol:
+            exempt += 1
+            continue
+        bad.append((t, s, "idx", int(got_idx[t, s]), int(ref_idx[t, s]), s_got, s_ref))
+    assert not bad, f"{what}: {len(bad)} slots break the parity rule, first: {bad[:5]}"
+    # Misses and non-searched slots carry index 0 (the reference's pre-zeroed outputs).
+    assert np.all(got_idx[~got_hit] == 0), f"{what}: a miss carries a nonzero index"
+    return exempt
+
+
+def check_combined(got, ref, what=""):
+    got = np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float32)
+    scale = float(np.max(np.abs(ref))) if ref.size else 0.0
+    err = np.abs(got - ref)
+    tol = COMBINE_RTOL * np.abs(ref) + COMBINE_RTOL * scale + 1e-12
+    assert np.all(err <= tol), f"{what}: combine max err {err.max()} (scale {scale})"
