@@ -1,0 +1,382 @@
+#!/usr/bin/env python
+"""ALUT lookup throughput on B200: the Qwen3-VL-30B-A3B-shaped decode step.
+
+Workload (one "step"): 48 MoE layers, each with 128 experts x 2 modalities of
+K=1024 x L=64 fp32 centroid keys and 1024 x 2048 bf16 value rows (random init, seeded);
+16 decode tokens (text), top-8 softmax routing over Gaussian logits, a seeded 40% of the
+routed (token, expert) slots looked up (the rest are "computed"). Per layer: project the
+tokens onto the layer's PCA basis, scan every routed table for the best centroid
+(normalised keys, hit = max >= 0: the tablemoe decode rule), gather the winning value
+rows and accumulate them, renormalised over the surviving slots, into the layer output.
+The layers run one after the other, as in a real decode step.
+
+value: lookups/s with inputs resident in HBM, the 48 layers replayed as one CUDA graph.
+e2e:   the same through the public LookupStepGraph API with the step's inputs copied
+       host->device and the outputs device->host inside the graph (pinned buffers).
+--impl reference: the CPU oracle (a restatement of the reference's torch path) on the
+       host cores, over a bounded sample of the same workload.
+
+N>1: one process per GPU, each a replica with its own tables and token batch (the decode
+lookup does not shard: "replicas only"); value is the sum over ranks of lookups divided
+by the max over ranks of the device time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (ROOT, ROOT / "tablemoe-sc26_b200"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+CFG = dict(layers=48, experts=128, k=1024, l=64, h=2048, tokens=16, top_k=8, lookup_frac=0.4)
+METRIC = "ALUT lookups/s (token-expert pairs)"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+KERNELS_PER_LAYER = 3  # project+plan, centroid scan, gather/combine
+CPU_LAYERS = 4
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def layer_inputs(layer: int, rank: int):
+    """Seeded synthetic inputs of one layer (host tensors)."""
+    g = torch.Generator().manual_seed(1000 * rank + layer)
+    q, s, e, h = CFG["tokens"], CFG["top_k"], CFG["experts"], CFG["h"]
+    x = torch.randn(q, h, generator=g).to(torch.bfloat16)
+    logits = torch.randn(q, e, generator=g)
+    w, sel = torch.topk(torch.softmax(logits, dim=-1), s, dim=-1)
+    reuse = torch.rand(q, s, generator=g) < CFG["lookup_frac"]
+    return dict(x=x, sel=sel.long(), is_vision=torch.zeros(q, dtype=torch.bool), reuse=reuse,
+                weights=w.float(), compute=~reuse)
+
+
+def build_layer(layer: int, device, rank: int):
+    """One layer's tables on the device: normalised keys (also passed as the raw keys: the
+    decode rule scores normalised keys only), bf16 values, orthonormal fp32 PCA basis."""
+    from table_moe.cache_engine import HybridStorageManager
+    from table_moe.cache_engine.manager import normalize_rows
+
+    e, k, l, h = CFG["experts"], CFG["k"], CFG["l"], CFG["h"]
+    g = torch.Generator(device=device).manual_seed(7919 * (rank + 1) + layer)
+    keys = normalize_rows(torch.randn(e, 2, k, l, generator=g, device=device), 1e-6)
+    values = torch.randn(e, 2, k, h, generator=g, device=device, dtype=torch.bfloat16).mul_(0.05)
+    pca = {}
+    for m in ("vision", "text"):
+        qm, _ = torch.linalg.qr(torch.randn(h, l, generator=g, device=device))
+        pca[m] = {"proj": qm.contiguous(), "bias": torch.zeros(l, device=device)}
+    return HybridStorageManager.from_tables(layer, keys, values, pca, keys=keys)
+
+
+def algorithmic_bytes(inp):
+    """Bytes one layer's lookup must move at minimum: the keys of every routed table once,
+    the winning value rows, x, the output read+write and the basis of the modality used.
+    Returns (scan kernel bytes, whole-path bytes, lookups)."""
+    k, l, h = CFG["k"], CFG["l"], CFG["h"]
+    r = inp["reuse"]
+    tables = len(set(inp["sel"][r].tolist()))  # all tokens are text: one modality
+    scan = tables * k * l * 4
+    lookups = int(r.sum())
+    rest = lookups * h * 2 + inp["x"].numel() * 2 + 2 * inp["x"].numel() * 2 + h * l * 4
+    return scan, scan + rest, lookups
+
+
+class ClockSampler:
+    """nvidia-smi samples (SM clock, throttle reasons) while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(self.NAMES, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"])}, "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v, world, device):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- CPU arms: the oracle (test infrastructure) timed as the baseline -----------------
+
+def cpu_sample(managers, inputs):
+    """Host copies of the sampled layers' tables and inputs for the oracle."""
+    from oracle import oracle as orc
+
+    sample = []
+    for m, inp in zip(managers, inputs):
+        keys = m.keys_buffer.float().cpu().numpy()
+        vals = m.values_buffer.cpu().view(torch.int16).numpy().view(np.uint16)
+        proj = np.stack([m.pca["vision"]["proj"].cpu().numpy(), m.pca["text"]["proj"].cpu().numpy()])
+        bias = np.stack([m.pca["vision"]["bias"].cpu().numpy(), m.pca["text"]["bias"].cpu().numpy()])
+        d = {k: v.numpy() for k, v in inp.items() if k != "x"}
+        d["x"] = inp["x"].float().numpy()
+        sample.append((keys, vals, proj, bias, d))
+    return orc, sample
+
+
+def cpu_step(orc, sample):
+    """One oracle pass over the sampled layers: project, search (normalised keys, >= 0),
+    combine (renormalised to one). Returns the lookups processed."""
+    n = 0
+    for keys, vals, proj, bias, inp in sample:
+        q = orc.project(inp["x"], inp["is_vision"], proj, bias)
+        hit, idx, _, _ = orc.search(q, keys, inp["sel"], inp["is_vision"], inp["reuse"], 0.0, 0.0, cmp_ge=True,
+                                    with_gap=False)
+        orc.combine(vals, inp["sel"], inp["is_vision"], hit, idx, inp["weights"], compute=inp["compute"], renorm=1)
+        n += int(inp["reuse"].sum())
+    return n
+
+
+def time_cpu(orc, sample, *, seconds=None, steps=None, warmup=1):
+    cores = len(os.sched_getaffinity(0))
+    orc.set_threads(cores)
+    for _ in range(warmup):
+        cpu_step(orc, sample)
+    t0 = time.perf_counter()
+    n = done = 0
+    while True:
+        n += cpu_step(orc, sample)
+        done += 1
+        dt = time.perf_counter() - t0
+        if (seconds is not None and dt >= seconds) or (steps is not None and done >= steps):
+            break
+    return n / dt, cores, done, dt
+
+
+def config_dict(world):
+    return {"workload": "qwen3-vl-30b-a3b decode step (BASELINE config 2)", "layers": CFG["layers"],
+            "experts": CFG["experts"], "centroids": CFG["k"], "pca_rank": CFG["l"], "hidden": CFG["h"],
+            "tokens_per_gpu": CFG["tokens"], "top_k": CFG["top_k"], "lookup_frac": CFG["lookup_frac"],
+            "key_dtype": "float32", "value_dtype": "bfloat16", "search": "normalised keys, hit = max >= 0",
+            "l2": "inputs larger than L2 (about 0.57 GB of keys and rows touched per step, 55 GB of tables)",
+            "parallelism": f"replicas x{world}"}
+
+
+def run_reference(args, rank, world, device):
+    """CPU oracle arm: rank 0 only, all host threads, bounded sample per step."""
+    if rank != 0:
+        return
+    managers = [build_layer(li, device, rank) for li in range(CPU_LAYERS)]
+    inputs = [layer_inputs(li, rank) for li in range(CPU_LAYERS)]
+    torch.cuda.synchronize()
+    orc, sample = cpu_sample(managers, inputs)
+    v, cores, steps, dt = time_cpu(orc, sample, steps=args.steps, warmup=args.warmup)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": "lookups/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random tables and routing)", "config": config_dict(world),
+            "cpu_baseline": {"value": round(v, 1), "unit": "lookups/s", "cores": cores, "kind": "port",
+                             "sample": f"each step = layers 0-{CPU_LAYERS - 1} of the decode step through the CPU "
+                                       "oracle (C restatement of the reference torch path)"},
+            "e2e": {"value": round(v, 1), "unit": "lookups/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["alut", "reference"], default="alut")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=device)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world, device)
+        else:
+            run_alut(args, rank, world, local, device)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+def run_alut(args, rank, world, local, device):
+    from table_moe.cache_engine import VectorSearchEngine
+    from table_moe.cache_engine.step_graph import LookupStepGraph
+
+    managers = [build_layer(li, device, rank) for li in range(CFG["layers"])]
+    engines = [VectorSearchEngine(m) for m in managers]
+    inputs = [layer_inputs(li, rank) for li in range(CFG["layers"])]
+    torch.cuda.synchronize()
+    per_layer = [algorithmic_bytes(inp) for inp in inputs]
+    scan_bytes = [p[0] for p in per_layer]
+    path_bytes = sum(p[1] for p in per_layer)
+    lookups_per_step = sum(p[2] for p in per_layer)
+
+    # Device-resident step, with per-layer scan-kernel events inside the graph.
+    step = LookupStepGraph(engines, CFG["tokens"], CFG["top_k"], variant="decode", renorm="to_one")
+    for b, inp in zip(step.layers, inputs):
+        for name, t in inp.items():
+            getattr(b, name).copy_(t)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in engines]
+    for a, b in ev:  # the CUDA events must exist before capture
+        a.record()
+        b.record()
+    torch.cuda.synchronize()
+    step.capture(profile_events=ev)
+    for _ in range(args.warmup):
+        step.replay()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            step.replay()
+        stop.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    scan_ms = step.scan_times_ms()  # per-layer scan kernels of the last timed step
+    dev_ms = max_over_ranks(start.elapsed_time(stop), world, device)
+    ms_per_step = dev_ms / args.steps
+    total_lookups = lookups_per_step * args.steps * world
+    value = total_lookups / (dev_ms / 1e3)
+
+    # End to end through the public API: H2D inputs + lookups + D2H outputs per step.
+    e2e = LookupStepGraph(engines, CFG["tokens"], CFG["top_k"], variant="decode", renorm="to_one")
+    for hb, inp in zip(e2e.host_layers, inputs):
+        for name, t in inp.items():
+            getattr(hb, name).copy_(t)
+    e2e.capture(with_copies=True)
+    for _ in range(args.warmup):
+        e2e.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        e2e.replay()
+    t2.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(s2.elapsed_time(t2), world, device)
+
+    peaks, peak_src = measured_peaks()
+    roofline = None
+    if scan_ms:
+        avg_ms = sum(scan_ms) / len(scan_ms)
+        bpl = sum(scan_bytes) / len(scan_bytes)
+        achieved = bpl / (avg_ms / 1e3) / 1e9
+        roofline = {"kernel": "k_search (centroid scan)", "bound": "hbm", "achieved": round(achieved, 1),
+                    "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                    "traffic": None, "peak_source": peak_src, "bytes_per_launch": int(bpl),
+                    "launch_us": round(avg_ms * 1e3, 2), "launches_timed": len(scan_ms)}
+    path_gbs = path_bytes / (ms_per_step / 1e3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        orc, sample = cpu_sample(managers[:CPU_LAYERS], inputs[:CPU_LAYERS])
+        v, cores, n, secs = time_cpu(orc, sample, seconds=args.cpu_seconds)
+        cpu = {"value": round(v, 1), "unit": "lookups/s", "cores": cores, "kind": "port",
+               "sample": f"CPU oracle (C restatement of the reference torch path) over layers 0-{CPU_LAYERS - 1} "
+                         f"of the step, {n} passes in {secs:.1f} s"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "lookups/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random tables and routing)", "config": config_dict(world),
+            "lookups_per_step": lookups_per_step * world,
+            "e2e": {"value": round(total_lookups / (e2e_ms / 1e3), 1), "unit": "lookups/s",
+                    "h2d_bytes_per_step": e2e.h2d_bytes, "d2h_bytes_per_step": e2e.d2h_bytes,
+                    "ms_per_step": round(e2e_ms / args.steps, 5)},
+            "gpu_launches": KERNELS_PER_LAYER * CFG["layers"] * args.steps,
+            "roofline": roofline,
+            "path_roofline": {"bytes_per_step": path_bytes, "achieved_gbs": round(path_gbs, 1),
+                              "frac": round(path_gbs / peaks["hbm_gbs"], 4), "peak_source": peak_src},
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -191,6 +191,13 @@ int alut_merge_packed(int32_t world, int32_t q, int32_t s, const uint64_t* packe
                       const uint8_t* is_vision, const alut_search_params_t* params,
                       uint8_t* out_hit, int64_t* out_idx, alut_stream_t stream);
 
+/* Profiling hook: when both events are set (cudaEvent_t handles), every following
+ * centroid-scan launch made by this thread is bracketed by event records on its stream
+ * (as external event nodes when the stream is being captured into a CUDA graph), so the
+ * caller can time that kernel alone with cudaEventElapsedTime. Pass NULL, NULL to stop.
+ * The events are not owned by the library. */
+int alut_set_profile_events(void* start_event, void* stop_event);
+
 /* Text of the last error seen by this thread (never NULL). */
 const char* alut_last_error(void);
 

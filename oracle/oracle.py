@@ -102,8 +102,8 @@ def project(x, is_vision, proj, bias, dtype="float32", normalize=False, eps=1e-6
 
 
 def search(q_low, keys, sel, is_vision, reuse=None, thr_vision=0.0, thr_text=0.0, cmp_ge=True,
-           dtype="float32"):
-    """Returns (hit [Q,S] bool, idx [Q,S] int64, best [Q,S] f32, gap [Q,S] f64)."""
+           dtype="float32", with_gap=True):
+    """Returns (hit [Q,S] bool, idx [Q,S] int64, best [Q,S] f32, gap [Q,S] f64 or None)."""
     q_low = _c(q_low, np.float32)
     keys = _c(keys, np.float32)
     sel = _c(sel, np.int64)
@@ -114,7 +114,7 @@ def search(q_low, keys, sel, is_vision, reuse=None, thr_vision=0.0, thr_text=0.0
     hit = np.zeros((Q, S), np.uint8)
     idx = np.zeros((Q, S), np.int64)
     best = np.empty((Q, S), np.float32)
-    gap = np.empty((Q, S), np.float64)
+    gap = np.empty((Q, S), np.float64) if with_gap else None
     lib().oracle_search(Q, S, E, K, L, _ptr(q_low), _ptr(keys), _ptr(sel), _ptr(vis), _ptr(ru),
                         float(thr_vision), float(thr_text), int(bool(cmp_ge)), ROUND[dtype],
                         _ptr(hit), _ptr(idx), _ptr(best), _ptr(gap))

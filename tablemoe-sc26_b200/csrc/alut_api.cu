@@ -15,6 +15,8 @@
 namespace alut {
 
 static thread_local char g_err[512] = "no error";
+static thread_local cudaEvent_t g_prof_start = nullptr;
+static thread_local cudaEvent_t g_prof_stop = nullptr;
 
 static int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -260,7 +262,17 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
                    (t->key_stride[1] * esz) % 16 == 0 && (t->key_stride[2] * esz) % 16 == 0;
   const int64_t max_tiles = w.max_groups * s.nchunks;
   const int grid = static_cast<int>(std::min<int64_t>(max_tiles, static_cast<int64_t>(num_sms()) * 8));
-  return launch_search(t->key_dtype, vec, s, std::max(grid, 1), search_smem_bytes(t->l), st);
+  if (g_prof_start && g_prof_stop) {
+    cudaError_t e = cudaEventRecordWithFlags(g_prof_start, st, cudaEventRecordExternal);
+    if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
+  }
+  rc = launch_search(t->key_dtype, vec, s, std::max(grid, 1), search_smem_bytes(t->l), st);
+  if (rc) return rc;
+  if (g_prof_start && g_prof_stop) {
+    cudaError_t e = cudaEventRecordWithFlags(g_prof_stop, st, cudaEventRecordExternal);
+    if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
+  }
+  return ALUT_OK;
 }
 
 static void fill_value_strides(const alut_tables_t* t, CombineArgs& c) {
@@ -287,6 +299,14 @@ using namespace alut;
 extern "C" {
 
 int alut_version(void) { return 100; }
+
+int alut_set_profile_events(void* start_event, void* stop_event) {
+  if ((start_event == nullptr) != (stop_event == nullptr))
+    return fail(ALUT_EINVAL, "profile events must be both set or both NULL");
+  g_prof_start = static_cast<cudaEvent_t>(start_event);
+  g_prof_stop = static_cast<cudaEvent_t>(stop_event);
+  return ALUT_OK;
+}
 
 const char* alut_last_error(void) { return g_err; }
 

@@ -74,6 +74,7 @@ SIGNATURES = {
                                            _I32, _P, _P, _I64, _P, _SZ, _P]),
     "alut_search_packed": (ctypes.c_int, [_TP, _BP, _PP, _P, _I64, _P, _P, _SZ, _P]),
     "alut_merge_packed": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _PP, _P, _P, _P]),
+    "alut_set_profile_events": (ctypes.c_int, [_P, _P]),
     "alut_last_error": (ctypes.c_char_p, []),
     "alut_version": (ctypes.c_int, []),
 }
@@ -178,6 +179,8 @@ def make_tables(keys, raw_keys, values, proj_vis, bias_vis, proj_txt, bias_txt) 
         t.bias[0], t.bias[1] = bias_vis.data_ptr(), bias_txt.data_ptr()
         t.proj_dtype = dtype_code(proj_vis.dtype)
         t.proj_stride_h = proj_vis.stride(0)
+        if values is not None and values.shape[3] != proj_vis.shape[0]:
+            raise ValueError(f"values hidden size {values.shape[3]} != projection rows {proj_vis.shape[0]}")
         t.h = proj_vis.shape[0]
     else:
         t.proj_dtype = t.key_dtype

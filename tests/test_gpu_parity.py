@@ -209,7 +209,7 @@ def test_16bit_tables_match_oracle(kdt):
 
 @pytest.mark.parametrize("L,K", [(12, 7), (20, 129), (8, 1), (256, 300)])
 def test_ragged_sizes_match_oracle(L, K):
-    s = synth(Q=37, S=3, E=5, K=K, L=L, H=72, seed=L + K, reuse_p=0.7)
+    s = synth(Q=37, S=3, E=5, K=K, L=L, H=max(72, L + 8), seed=L + K, reuse_p=0.7)
     mgr = synth_manager(s)
     hit, idx = gpu_dot(mgr, s)
     q, keys, rh, ri = oracle_dot(s)
@@ -223,12 +223,12 @@ def test_ties_take_the_first_index_across_chunks():
     raw = torch.randn(1, 2, 1000, 16) * 0.01
     for t in range(8):
         m = 0 if bool(s["vis"][t]) else 1
-        for k in (900 - t, 300 + t, 131):  # duplicates in three different 128-centroid chunks
+        for k in (900 - t, 300 + t, 131 + t):  # duplicates in three different 128-centroid chunks
             raw[0, m, k] = torch.from_numpy(q[t]) * 3
     s["raw"] = raw
     hit, idx = gpu_dot(synth_manager(s), s)
     assert hit.all()
-    assert idx[:, 0].cpu().tolist() == [131] * 8
+    assert idx[:, 0].cpu().tolist() == [131 + t for t in range(8)]
 
 
 def test_edge_cases_empty_no_reuse_bad_ids():
