@@ -256,9 +256,12 @@ def main():
     ap.add_argument("--impl", choices=["alut", "reference"], default="alut")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=CFG["layers"],
+                    help="fewer layers for profiling captures only (the benchmark is 48)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    CFG["layers"] = args.layers
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)

@@ -125,6 +125,24 @@ static int check_params(const alut_tables_t* t, const alut_search_params_t* p, c
 
 // ---- launches ------------------------------------------------------------------------
 
+// Launch as a programmatic dependent of the previous kernel in the stream (it may start
+// early and waits in griddepcontrol.wait for the predecessor's results).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <typename TX, typename TK>
 static int launch_project_plan_t(const ProjPlanArgs& a, int grid, size_t smem, cudaStream_t st) {
   auto kern = k_project_plan<TX, TK, TK>;
@@ -179,11 +197,49 @@ static int launch_search(int key_dtype, bool vec, const SearchArgs& a, int grid,
   return fail(ALUT_EDTYPE, "key dtype");
 }
 
+template <typename TK>
+static int launch_search_tma_t(const SearchArgs& a, int grid, size_t smem, int* err, cudaStream_t st) {
+  int rc = allow_smem(reinterpret_cast<const void*>(k_search_tma<TK>), smem);
+  if (rc) return rc;
+  k_search_tma<TK><<<grid, kSearchThreads, smem, st>>>(a, err);
+  return check_launch("k_search_tma");
+}
+
+static int launch_search_tma(int key_dtype, const SearchArgs& a, int grid, size_t smem, int* err,
+                             cudaStream_t st) {
+  switch (key_dtype) {
+    case ALUT_F32: return launch_search_tma_t<float>(a, grid, smem, err, st);
+    case ALUT_BF16: return launch_search_tma_t<__nv_bfloat16>(a, grid, smem, err, st);
+    case ALUT_F16: return launch_search_tma_t<__half>(a, grid, smem, err, st);
+  }
+  return fail(ALUT_EDTYPE, "key dtype");
+}
+
 template <typename TV, typename TO>
 static int launch_combine_t(bool vec, const CombineArgs& a, dim3 grid, cudaStream_t st) {
-  if (vec) k_combine<TV, TO, true><<<grid, kCombineThreads, 0, st>>>(a);
-  else k_combine<TV, TO, false><<<grid, kCombineThreads, 0, st>>>(a);
+  cudaError_t e = vec ? launch_pdl(k_combine<TV, TO, true>, grid, dim3(kCombineThreads), 0, st, a)
+                      : launch_pdl(k_combine<TV, TO, false>, grid, dim3(kCombineThreads), 0, st, a);
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "k_combine: %s", cudaGetErrorString(e));
   return check_launch("k_combine");
+}
+
+template <typename TK>
+static int launch_search_decode_t(const DecodeScanArgs& d, dim3 grid, size_t smem, cudaStream_t st) {
+  int rc = allow_smem(reinterpret_cast<const void*>(k_search_decode<TK>), smem);
+  if (rc) return rc;
+  cudaError_t e = launch_pdl(k_search_decode<TK>, grid, dim3(kSearchThreads), smem, st, d);
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "k_search_decode: %s", cudaGetErrorString(e));
+  return check_launch("k_search_decode");
+}
+
+static int launch_search_decode(int key_dtype, const DecodeScanArgs& d, dim3 grid, size_t smem,
+                                cudaStream_t st) {
+  switch (key_dtype) {
+    case ALUT_F32: return launch_search_decode_t<float>(d, grid, smem, st);
+    case ALUT_BF16: return launch_search_decode_t<__nv_bfloat16>(d, grid, smem, st);
+    case ALUT_F16: return launch_search_decode_t<__half>(d, grid, smem, st);
+  }
+  return fail(ALUT_EDTYPE, "key dtype");
 }
 
 static int launch_combine(int vd, int od, bool vec, const CombineArgs& a, dim3 grid,
@@ -238,6 +294,51 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
   a.sorted = reinterpret_cast<int*>(base + w.sorted);
   a.groups = reinterpret_cast<int4*>(base + w.groups);
   a.meta = reinterpret_cast<int*>(base + w.meta);
+  const int esz = dtype_size(t->key_dtype);
+  const bool vec = (t->l % 8 == 0) && aligned16(keys) && (t->key_stride[0] * esz) % 16 == 0 &&
+                   (t->key_stride[1] * esz) % 16 == 0 && (t->key_stride[2] * esz) % 16 == 0;
+  const bool tma = vec && t->key_stride[2] == t->l && static_cast<int64_t>(t->l) * esz <= 512;
+  const int pairs = b->q * b->s;
+  if (tma && b->q <= kDecodeMaxTokens && pairs <= kDecodeMaxPairs) {
+    // Decode: projection (which also clears `best`), then the scan as its programmatic
+    // dependent, whose key copies overlap the projection.
+    a.do_plan = 0;
+    a.zero_best = best;
+    a.zero_n = pairs;
+    if (g_prof_start && g_prof_stop) {
+      cudaError_t e = cudaEventRecordWithFlags(g_prof_start, st, cudaEventRecordExternal);
+      if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
+    }
+    int rc = launch_project_plan(t->key_dtype, b->x_dtype, a, a.qtiles * a.nsplit, proj_smem_bytes(t->l), st);
+    if (rc) return rc;
+    DecodeScanArgs d{};
+    d.s.keys = keys;
+    d.s.key_stride_e = t->key_stride[0];
+    d.s.key_stride_m = t->key_stride[1];
+    d.s.key_stride_k = t->key_stride[2];
+    d.s.k = t->k;
+    d.s.l = t->l;
+    d.s.s = b->s;
+    d.s.nchunks = ceil_div(t->k, kSearchChunkK);
+    d.s.idx_offset = idx_offset;
+    d.s.qlow = a.qlow;
+    d.s.best = best;
+    d.q = b->q;
+    d.num_experts = t->num_experts;
+    d.sel = b->sel;
+    d.sel_stride = b->sel_stride;
+    d.is_vision = b->is_vision;
+    d.reuse = b->reuse;
+    d.reuse_stride = b->reuse_stride;
+    d.err = a.meta + 1;
+    rc = launch_search_decode(t->key_dtype, d, dim3(pairs, d.s.nchunks), search_decode_smem_bytes(t->l, esz), st);
+    if (rc) return rc;
+    if (g_prof_start && g_prof_stop) {
+      cudaError_t e = cudaEventRecordWithFlags(g_prof_stop, st, cudaEventRecordExternal);
+      if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
+    }
+    return ALUT_OK;
+  }
   const size_t smem1 = std::max(proj_smem_bytes(t->l), plan_smem_bytes(2 * t->num_experts));
   int rc = launch_project_plan(t->key_dtype, b->x_dtype, a, a.qtiles * a.nsplit + 1, smem1, st);
   if (rc) return rc;
@@ -257,16 +358,18 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
   s.groups = a.groups;
   s.meta = a.meta;
   s.best = best;
-  const int esz = dtype_size(t->key_dtype);
-  const bool vec = (t->l % 8 == 0) && aligned16(keys) && (t->key_stride[0] * esz) % 16 == 0 &&
-                   (t->key_stride[1] * esz) % 16 == 0 && (t->key_stride[2] * esz) % 16 == 0;
   const int64_t max_tiles = w.max_groups * s.nchunks;
   const int grid = static_cast<int>(std::min<int64_t>(max_tiles, static_cast<int64_t>(num_sms()) * 8));
   if (g_prof_start && g_prof_stop) {
     cudaError_t e = cudaEventRecordWithFlags(g_prof_start, st, cudaEventRecordExternal);
     if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
   }
-  rc = launch_search(t->key_dtype, vec, s, std::max(grid, 1), search_smem_bytes(t->l), st);
+  if (tma) {
+    rc = launch_search_tma(t->key_dtype, s, std::max(grid, 1), search_tma_smem_bytes(t->l, esz),
+                           reinterpret_cast<int*>(a.meta) + 1, st);
+  } else {
+    rc = launch_search(t->key_dtype, vec, s, std::max(grid, 1), search_smem_bytes(t->l), st);
+  }
   if (rc) return rc;
   if (g_prof_start && g_prof_stop) {
     cudaError_t e = cudaEventRecordWithFlags(g_prof_stop, st, cudaEventRecordExternal);
@@ -395,7 +498,8 @@ int alut_search(const alut_tables_t* tables, const alut_batch_t* batch,
   f.out_idx = out_idx;
   f.out_stride = out_stride;
   const int64_t n = static_cast<int64_t>(batch->q) * batch->s;
-  k_finalize<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(f);
+  cudaError_t e = launch_pdl(k_finalize, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, st, f);
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "k_finalize: %s", cudaGetErrorString(e));
   return check_launch("k_finalize");
 }
 

@@ -39,6 +39,7 @@ struct CombineArgs {
 };
 
 constexpr int kCombineSpan = kCombineThreads * 8;
+static_assert(kMaxSlots <= kCombineThreads, "one slot per thread in the combine prologue");
 
 template <typename TV, typename TO, bool kVec>
 __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
@@ -51,11 +52,24 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
   __shared__ int s_n;
   const int tid = threadIdx.x;
   const int t = blockIdx.x;
+  pdl_launch_dependents();
+  // Inputs first (they do not depend on the search), then wait for the search results.
+  bool r_ = false, ev_ = false, comp_ = false;
+  int64_t e_ = 0;
+  float w_ = 0.f;
+  const int m = a.is_vision[t] ? 0 : 1;
+  if (tid < a.s) {
+    r_ = a.reuse ? (a.reuse[t * a.reuse_stride + tid] != 0) : true;
+    e_ = a.sel[t * a.sel_stride + tid];
+    ev_ = e_ >= 0 && e_ < a.num_experts;
+    comp_ = a.compute ? (a.compute[t * a.compute_stride + tid] != 0) : false;
+    w_ = a.w[t * a.w_stride + tid];
+  }
+  pdl_wait();
   for (int s = tid; s < a.s; s += kCombineThreads) {
-    const bool r = a.reuse ? (a.reuse[t * a.reuse_stride + s] != 0) : true;
-    const int64_t e = a.sel[t * a.sel_stride + s];
-    const bool ev = e >= 0 && e < a.num_experts;
-    const int m = a.is_vision[t] ? 0 : 1;
+    const bool r = r_;
+    const int64_t e = e_;
+    const bool ev = ev_;
     bool hit = false;
     int64_t idx = 0;
     if (a.best) {
@@ -74,9 +88,9 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
       a.out_hit[t * a.out_hit_stride + s] = hit ? 1 : 0;
       a.out_idx[t * a.out_hit_stride + s] = hit ? idx : 0;
     }
-    const bool comp = a.compute ? (a.compute[t * a.compute_stride + s] != 0) : false;
+    const bool comp = comp_;
     const bool look = hit && ev && idx >= 0 && idx < a.k;
-    s_w[s] = a.w[t * a.w_stride + s];
+    s_w[s] = w_;
     s_surv[s] = (comp || hit) ? 1 : 0;
     s_look[s] = look ? 1 : 0;
     s_off[s] = look ? (e * a.vs_e + m * a.vs_m + idx * a.vs_k) : 0;

@@ -13,7 +13,7 @@ namespace alut {
 
 // Tokens per projection tile, centroids per search tile, query slots per search group.
 constexpr int kProjTileQ = 16;
-constexpr int kProjChunkH = 16;
+constexpr int kProjChunkH = 64;
 constexpr int kProjThreads = 256;
 constexpr int kMaxL = 256;               // L <= kMaxL (outputs per projection thread <= 16)
 constexpr int kSearchThreads = 128;      // one centroid per thread
@@ -110,6 +110,27 @@ template <typename T> __device__ __forceinline__ void load8_rw(const T* p, float
   for (int i = 0; i < 8; ++i) o[i] = to_f32<T>(p[i]);
 }
 
+// ---- cp.async (16-byte global -> shared copies, waited per commit group) -----------------
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ---- programmatic dependent launch --------------------------------------------------------
+// A kernel launched with the programmatic-stream-serialization attribute may start while
+// its predecessor in the stream is still running; griddepcontrol.wait blocks until the
+// predecessor has completed and its memory is visible (a no-op without the attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- packed candidates -------------------------------------------------------------
 // A candidate (score, index) is packed into 64 bits so that unsigned max picks the
 // larger score and, among equal scores, the smaller index (search.py:89 / torch.max).
@@ -165,7 +186,7 @@ struct Workspace {
   int64_t max_groups;
 };
 
-inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+__host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 inline int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
@@ -173,8 +194,11 @@ inline int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) 
 // that a decode batch still spreads over the whole GPU).
 inline int proj_splits(int q, int h) {
   int qtiles = ceil_div(q, kProjTileQ);
-  int max_split = ceil_div(h, kProjChunkH);
+  // At least 2 basis chunks (128 rows of H) per split, so that the split partials stay few
+  // and the chunk pipeline has something to overlap.
+  int max_split = ceil_div(h, 2 * kProjChunkH);
   if (max_split > 64) max_split = 64;
+  if (max_split < 1) max_split = 1;
   int s = kProjSplitTarget / (qtiles > 0 ? qtiles : 1);
   if (s < 1) s = 1;
   if (s > max_split) s = max_split;

@@ -36,17 +36,25 @@ struct ProjPlanArgs {
   int* sorted;
   int4* groups;
   int* meta;
+  // decode path: zero best[0, zero_n) (no planning CTA)
+  uint64_t* zero_best;
+  int zero_n;
 };
 
 constexpr int kProjOutPerThread = (kProjTileQ * kMaxL) / kProjThreads;  // 16
 
-// Dynamic shared memory of one projection CTA: the two modalities' basis chunks, then the
-// token chunk; the chunk area is reused for the output tile.
+// Dynamic shared memory of one projection CTA: two pipeline buffers, each holding both
+// modalities' basis chunk [kProjChunkH][L] and the token chunk [kProjTileQ][kProjChunkH] in
+// their storage dtypes (<= 4 bytes); the area is reused for the fp32 output tile.
+// Basis rows per pipeline chunk: 64, or 32 when L > 128 so two buffers fit in 227 KB.
+__host__ __device__ inline int proj_chunk_rows(int l) { return l > 128 ? kProjChunkH / 2 : kProjChunkH; }
+__host__ __device__ inline size_t proj_buffer_bytes(int l) {
+  const int hc = proj_chunk_rows(l);
+  return align256(sizeof(float) * (2 * hc * l + kProjTileQ * hc));
+}
 inline size_t proj_smem_bytes(int l) {
-  size_t ps = sizeof(float) * 2 * kProjChunkH * l;
-  size_t xs = sizeof(float) * kProjTileQ * kProjChunkH;
+  size_t a = 2 * proj_buffer_bytes(l);
   size_t tile = sizeof(float) * kProjTileQ * l;
-  size_t a = ps + xs;
   return a > tile ? a : tile;
 }
 inline size_t plan_smem_bytes(int num_tables) { return sizeof(int) * 3 * num_tables; }
@@ -173,7 +181,10 @@ __device__ void finish_tile(const ProjPlanArgs& a, float* tile, int q0, int nq,
 
 template <typename TX, typename TP, typename TK>
 __global__ void __launch_bounds__(kProjThreads) k_project_plan(ProjPlanArgs a) {
-  extern __shared__ __align__(16) float smem[];
+  extern __shared__ __align__(256) float smem[];
+  pdl_launch_dependents();
+  if (a.zero_best && blockIdx.x == 0)
+    for (int i = threadIdx.x; i < a.zero_n; i += kProjThreads) a.zero_best[i] = 0ull;
   const int nproj = a.qtiles * a.nsplit;
   if (a.do_plan && static_cast<int>(blockIdx.x) == nproj) {
     plan_pairs(a, reinterpret_cast<int*>(smem));
@@ -210,8 +221,9 @@ __global__ void __launch_bounds__(kProjThreads) k_project_plan(ProjPlanArgs a) {
     return;
   }
 
-  float* ps = smem;                                   // [2][kProjChunkH][L]
-  float* xs = smem + 2 * kProjChunkH * L;             // [kProjTileQ][kProjChunkH]
+  // Basis and token chunks stream through two shared-memory buffers with cp.async
+  // (16-byte copies when rows are 16-byte multiples and aligned, else 4-byte ones or plain
+  // loads), so the next chunk is in flight while this one is multiplied.
   const int nout = (kProjTileQ * L + kProjThreads - 1) / kProjThreads;
   float acc[kProjOutPerThread];
   int oq[kProjOutPerThread], ol[kProjOutPerThread];
@@ -222,42 +234,86 @@ __global__ void __launch_bounds__(kProjThreads) k_project_plan(ProjPlanArgs a) {
     oq[i] = o / L;
     ol[i] = o % L;
   }
-  const int nch = (a.h + kProjChunkH - 1) / kProjChunkH;
+  const int HC = proj_chunk_rows(L);
+  const int nch = (a.h + HC - 1) / HC;
   const int c_begin = static_cast<int>(static_cast<int64_t>(sp) * nch / a.nsplit);
   const int c_end = static_cast<int>(static_cast<int64_t>(sp + 1) * nch / a.nsplit);
   const TX* x = static_cast<const TX*>(a.x);
-  for (int c = c_begin; c < c_end; ++c) {
-    const int h0 = c * kProjChunkH;
-    const int hn = min(kProjChunkH, a.h - h0);
-    __syncthreads();
+  const size_t buf_bytes = proj_buffer_bytes(L);
+  const bool p_vec = (L * sizeof(TP)) % 16 == 0 && (a.proj_stride * sizeof(TP)) % 16 == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.proj[0]) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.proj[1]) & 15) == 0;
+  const bool x_vec = (HC * sizeof(TX)) % 16 == 0 && (a.x_stride * sizeof(TX)) % 16 == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.h * sizeof(TX)) % 16 == 0;
+  auto stage = [&](int c, int b) {
+    unsigned char* base = reinterpret_cast<unsigned char*>(smem) + b * buf_bytes;
+    TP* ps = reinterpret_cast<TP*>(base);                                   // [2][HC][L]
+    TX* xs = reinterpret_cast<TX*>(base + sizeof(float) * 2 * HC * L);  // [16][HC]
+    const int h0 = c * HC;
+    const int hn = min(HC, a.h - h0);
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
       if (!need[m]) continue;
-      const TP* p = static_cast<const TP*>(a.proj[m]);
-      for (int i = tid; i < kProjChunkH * L; i += kProjThreads) {
-        const int r = i / L, col = i % L;
-        ps[m * kProjChunkH * L + i] =
-            r < hn ? to_f32<TP>(p[static_cast<int64_t>(h0 + r) * a.proj_stride + col]) : 0.f;
+      const TP* pg = static_cast<const TP*>(a.proj[m]) + static_cast<int64_t>(h0) * a.proj_stride;
+      TP* pd = ps + m * HC * L;
+      if (p_vec) {
+        constexpr int kE = 16 / sizeof(TP);
+        const int per_row = L / kE;
+        for (int i = tid; i < hn * per_row; i += kProjThreads) {
+          const int r = i / per_row, u = i % per_row;
+          cp_async16(pd + r * L + u * kE, pg + static_cast<int64_t>(r) * a.proj_stride + u * kE);
+        }
+      } else {
+        for (int i = tid; i < hn * L; i += kProjThreads) {
+          const int r = i / L, col = i % L;
+          pd[r * L + col] = pg[static_cast<int64_t>(r) * a.proj_stride + col];
+        }
+      }
+      for (int i = hn * L + tid; i < HC * L; i += kProjThreads) pd[i] = TP(0.f);
+    }
+    if (x_vec && hn == HC) {
+      constexpr int kE = 16 / sizeof(TX);
+      const int per_row = HC / kE;
+      for (int i = tid; i < kProjTileQ * per_row; i += kProjThreads) {
+        const int r = i / per_row, u = i % per_row;
+        if (r < nq) cp_async16(xs + r * HC + u * kE, x + static_cast<int64_t>(q0 + r) * a.x_stride + h0 + u * kE);
+        else
+          for (int e = 0; e < kE; ++e) xs[r * HC + u * kE + e] = TX(0.f);
+      }
+    } else {
+      for (int i = tid; i < kProjTileQ * HC; i += kProjThreads) {
+        const int r = i / HC, col = i % HC;
+        xs[i] = (r < nq && col < hn) ? x[static_cast<int64_t>(q0 + r) * a.x_stride + h0 + col] : TX(0.f);
       }
     }
-    for (int i = tid; i < kProjTileQ * kProjChunkH; i += kProjThreads) {
-      const int r = i / kProjChunkH, col = i % kProjChunkH;
-      xs[i] = (r < nq && col < hn) ? to_f32<TX>(x[static_cast<int64_t>(q0 + r) * a.x_stride + h0 + col]) : 0.f;
+    cp_async_commit();
+  };
+  if (c_begin < c_end) stage(c_begin, 0);
+  for (int c = c_begin; c < c_end; ++c) {
+    const int b = (c - c_begin) & 1;
+    if (c + 1 < c_end) {
+      stage(c + 1, b ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
+    const unsigned char* base = reinterpret_cast<const unsigned char*>(smem) + b * buf_bytes;
+    const TP* ps = reinterpret_cast<const TP*>(base);
+    const TX* xs = reinterpret_cast<const TX*>(base + sizeof(float) * 2 * HC * L);
 #pragma unroll
     for (int i = 0; i < kProjOutPerThread; ++i) {
       if (i < nout && oq[i] < kProjTileQ) {
-        const float* prow = ps + mod[oq[i]] * kProjChunkH * L + ol[i];
-        const float* xrow = xs + oq[i] * kProjChunkH;
+        const TP* prow = ps + mod[oq[i]] * HC * L + ol[i];
+        const TX* xrow = xs + oq[i] * HC;
         float v = acc[i];
-#pragma unroll
-        for (int hh = 0; hh < kProjChunkH; ++hh) v = fmaf(xrow[hh], prow[hh * L], v);
+#pragma unroll 16
+        for (int hh = 0; hh < HC; ++hh) v = fmaf(to_f32<TX>(xrow[hh]), to_f32<TP>(prow[hh * L]), v);
         acc[i] = v;
       }
     }
+    __syncthreads();  // buffer b may be refilled by the next iteration's stage()
   }
-  __syncthreads();
   if (a.nsplit == 1) {
 #pragma unroll
     for (int i = 0; i < kProjOutPerThread; ++i)
@@ -276,9 +332,19 @@ __global__ void __launch_bounds__(kProjThreads) k_project_plan(ProjPlanArgs a) {
     if (tid == 0) a.counters[qt] = 0u;
     // The last CTA of the tile sums the partials in split order (deterministic).
     const float* base = a.qpart + static_cast<int64_t>(qt * a.nsplit) * kProjTileQ * L;
+    // Loads are issued 8 splits at a time (independent), then added in split order.
+    const int64_t stride = static_cast<int64_t>(kProjTileQ) * L;
     for (int i = tid; i < kProjTileQ * L; i += kProjThreads) {
       float v = 0.f;
-      for (int k = 0; k < a.nsplit; ++k) v += __ldcg(base + static_cast<int64_t>(k) * kProjTileQ * L + i);
+      int k = 0;
+      for (; k + 8 <= a.nsplit; k += 8) {
+        float p[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) p[u] = __ldcg(base + (k + u) * stride + i);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v += p[u];
+      }
+      for (; k < a.nsplit; ++k) v += __ldcg(base + k * stride + i);
       tile[i] = v;
     }
   }
