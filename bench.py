@@ -45,6 +45,7 @@ METRIC = "ALUT lookups/s (token-expert pairs)"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 KERNELS_PER_LAYER = 3  # project+plan, centroid scan, gather/combine
 CPU_LAYERS = 4
+PROFILE_STEPS = 20  # replays of the event-instrumented step graph for the scan-kernel timing
 
 
 def dist_env():
@@ -83,13 +84,13 @@ def build_layer(layer: int, device, rank: int):
 def algorithmic_bytes(inp):
     """Bytes one layer's lookup must move at minimum: the keys of every routed table once,
     the winning value rows, x, the output read+write and the basis of the modality used.
-    Returns (scan kernel bytes, whole-path bytes, lookups)."""
+    Returns (projection + scan bytes, whole-path bytes, lookups)."""
     k, l, h = CFG["k"], CFG["l"], CFG["h"]
     r = inp["reuse"]
     tables = len(set(inp["sel"][r].tolist()))  # all tokens are text: one modality
-    scan = tables * k * l * 4
+    scan = tables * k * l * 4 + h * l * 4 + inp["x"].numel() * 2  # keys + basis + tokens
     lookups = int(r.sum())
-    rest = lookups * h * 2 + inp["x"].numel() * 2 + 2 * inp["x"].numel() * 2 + h * l * 4
+    rest = lookups * h * 2 + 2 * inp["x"].numel() * 2  # value rows + output read/write
     return scan, scan + rest, lookups
 
 
@@ -294,17 +295,22 @@ def run_alut(args, rank, world, local, device):
     path_bytes = sum(p[1] for p in per_layer)
     lookups_per_step = sum(p[2] for p in per_layer)
 
-    # Device-resident step, with per-layer scan-kernel events inside the graph.
+    # Device-resident step (timed), and a twin graph whose scan launches are bracketed by
+    # event nodes (replayed after the timed region to time the scan kernels; event nodes
+    # break the programmatic overlap between kernels, so they stay out of the timed graph).
     step = LookupStepGraph(engines, CFG["tokens"], CFG["top_k"], variant="decode", renorm="to_one")
-    for b, inp in zip(step.layers, inputs):
-        for name, t in inp.items():
-            getattr(b, name).copy_(t)
+    prof = LookupStepGraph(engines, CFG["tokens"], CFG["top_k"], variant="decode", renorm="to_one")
+    for g in (step, prof):
+        for b, inp in zip(g.layers, inputs):
+            for name, t in inp.items():
+                getattr(b, name).copy_(t)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in engines]
     for a, b in ev:  # the CUDA events must exist before capture
         a.record()
         b.record()
     torch.cuda.synchronize()
-    step.capture(profile_events=ev)
+    step.capture()
+    prof.capture(profile_events=ev)
     for _ in range(args.warmup):
         step.replay()
     torch.cuda.synchronize()
@@ -318,11 +324,15 @@ def run_alut(args, rank, world, local, device):
         stop.record()
         torch.cuda.synchronize()
         barrier(world)
-    scan_ms = step.scan_times_ms()  # per-layer scan kernels of the last timed step
     dev_ms = max_over_ranks(start.elapsed_time(stop), world, device)
     ms_per_step = dev_ms / args.steps
     total_lookups = lookups_per_step * args.steps * world
     value = total_lookups / (dev_ms / 1e3)
+    scan_ms = []
+    for _ in range(PROFILE_STEPS):
+        prof.replay()
+        torch.cuda.synchronize()
+        scan_ms += prof.scan_times_ms()
 
     # End to end through the public API: H2D inputs + lookups + D2H outputs per step.
     e2e = LookupStepGraph(engines, CFG["tokens"], CFG["top_k"], variant="decode", renorm="to_one")
@@ -348,10 +358,12 @@ def run_alut(args, rank, world, local, device):
         avg_ms = sum(scan_ms) / len(scan_ms)
         bpl = sum(scan_bytes) / len(scan_bytes)
         achieved = bpl / (avg_ms / 1e3) / 1e9
-        roofline = {"kernel": "k_search (centroid scan)", "bound": "hbm", "achieved": round(achieved, 1),
+        roofline = {"kernel": "k_project + k_search_decode (projection + centroid scan)", "bound": "hbm", "achieved": round(achieved, 1),
                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                     "traffic": None, "peak_source": peak_src, "bytes_per_launch": int(bpl),
-                    "launch_us": round(avg_ms * 1e3, 2), "launches_timed": len(scan_ms)}
+                    "launch_us": round(avg_ms * 1e3, 2), "launches_timed": len(scan_ms),
+                    "timed_span": "projection + centroid scan (the scan is launched as a programmatic "
+                                  "dependent of the projection and streams keys while it runs)"}
     path_gbs = path_bytes / (ms_per_step / 1e3) / 1e9
 
     cpu = None

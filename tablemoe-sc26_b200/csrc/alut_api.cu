@@ -143,34 +143,94 @@ static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// Projection: grid = qtiles x nsplit CTAs; the nsplit CTAs of a token tile form one
+// thread-block cluster (they add their partial tiles through distributed shared memory).
 template <typename TX, typename TK>
-static int launch_project_plan_t(const ProjPlanArgs& a, int grid, size_t smem, cudaStream_t st) {
-  auto kern = k_project_plan<TX, TK, TK>;
+static int launch_project_t(const ProjPlanArgs& args, size_t smem, cudaStream_t st) {
+  ProjPlanArgs a = args;
+  const int nout = proj_nout(a.l);
+  auto kern = nout == 4 ? k_project<TX, TK, TK, 4> : (nout == 8 ? k_project<TX, TK, TK, 8> : k_project<TX, TK, TK, 16>);
   int rc = allow_smem(reinterpret_cast<const void*>(kern), smem);
   if (rc) return rc;
-  kern<<<grid, kProjThreads, smem, st>>>(a);
-  return check_launch("k_project_plan");
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kProjThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (a.nsplit > 8) {
+    // Clusters above 8 CTAs are non-portable: opt in once per device, and fall back to 8
+    // if this device cannot co-schedule that many CTAs of this size.
+    struct Known { const void* k; int dev; size_t smem; int ok; };
+    static Known known[128];
+    static int nknown = 0;
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int ok = -1;
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      for (int i = 0; i < nknown; ++i)
+        if (known[i].k == reinterpret_cast<const void*>(kern) && known[i].dev == dev && known[i].smem == smem)
+          ok = known[i].ok;
+    }
+    if (ok < 0) {
+      ok = 0;
+      if (cudaFuncSetAttribute(reinterpret_cast<const void*>(kern), cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+          cudaSuccess) {
+        cfg.gridDim = dim3(a.nsplit);
+        attr[0].val.clusterDim.x = a.nsplit;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, reinterpret_cast<const void*>(kern), &cfg) == cudaSuccess &&
+            clusters > 0)
+          ok = 1;
+      }
+      cudaGetLastError();
+      std::lock_guard<std::mutex> lock(mu);
+      if (nknown < 128) known[nknown++] = Known{reinterpret_cast<const void*>(kern), dev, smem, ok};
+    }
+    int* sd = nullptr;
+    int two = ok ? 1 : 2;
+    sd = &two;
+    if (sd && *sd == 2) a.nsplit = 8;
+  }
+  cfg.gridDim = dim3(a.qtiles * a.nsplit);
+  attr[0].val.clusterDim.x = a.nsplit;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "k_project: %s", cudaGetErrorString(e));
+  return check_launch("k_project");
 }
 
 template <typename TK>
-static int launch_project_plan_k(int x_dtype, const ProjPlanArgs& a, int grid, size_t smem,
-                                 cudaStream_t st) {
+static int launch_project_k(int x_dtype, const ProjPlanArgs& a, size_t smem, cudaStream_t st) {
   switch (x_dtype) {
-    case ALUT_F32: return launch_project_plan_t<float, TK>(a, grid, smem, st);
-    case ALUT_BF16: return launch_project_plan_t<__nv_bfloat16, TK>(a, grid, smem, st);
-    case ALUT_F16: return launch_project_plan_t<__half, TK>(a, grid, smem, st);
+    case ALUT_F32: return launch_project_t<float, TK>(a, smem, st);
+    case ALUT_BF16: return launch_project_t<__nv_bfloat16, TK>(a, smem, st);
+    case ALUT_F16: return launch_project_t<__half, TK>(a, smem, st);
   }
   return fail(ALUT_EDTYPE, "x dtype");
 }
 
-static int launch_project_plan(int key_dtype, int x_dtype, const ProjPlanArgs& a, int grid,
-                               size_t smem, cudaStream_t st) {
+static int launch_project(int key_dtype, int x_dtype, const ProjPlanArgs& a, cudaStream_t st) {
+  const size_t smem = proj_smem_bytes(a.l);
   switch (key_dtype) {
-    case ALUT_F32: return launch_project_plan_k<float>(x_dtype, a, grid, smem, st);
-    case ALUT_BF16: return launch_project_plan_k<__nv_bfloat16>(x_dtype, a, grid, smem, st);
-    case ALUT_F16: return launch_project_plan_k<__half>(x_dtype, a, grid, smem, st);
+    case ALUT_F32: return launch_project_k<float>(x_dtype, a, smem, st);
+    case ALUT_BF16: return launch_project_k<__nv_bfloat16>(x_dtype, a, smem, st);
+    case ALUT_F16: return launch_project_k<__half>(x_dtype, a, smem, st);
   }
   return fail(ALUT_EDTYPE, "key dtype");
+}
+
+static int launch_plan(const ProjPlanArgs& a, cudaStream_t st) {
+  const size_t smem = plan_smem_bytes(2 * a.num_experts);
+  int rc = allow_smem(reinterpret_cast<const void*>(k_plan), smem);
+  if (rc) return rc;
+  k_plan<<<1, kProjThreads, smem, st>>>(a);
+  return check_launch("k_plan");
 }
 
 template <typename TK>
@@ -280,10 +340,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
   a.nsplit = q_low_in ? 1 : proj_splits(b->q, t->h);
   a.normalize = p->normalize_q;
   a.eps = p->eps;
-  a.qpart = reinterpret_cast<float*>(base + w.qpart);
   a.qlow = reinterpret_cast<float*>(base + w.qlow);
-  a.counters = reinterpret_cast<uint32_t*>(base + w.counters);
-  a.do_plan = 1;
   a.s = b->s;
   a.num_experts = t->num_experts;
   a.sel = b->sel;
@@ -302,14 +359,13 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
   if (tma && b->q <= kDecodeMaxTokens && pairs <= kDecodeMaxPairs) {
     // Decode: projection (which also clears `best`), then the scan as its programmatic
     // dependent, whose key copies overlap the projection.
-    a.do_plan = 0;
     a.zero_best = best;
     a.zero_n = pairs;
     if (g_prof_start && g_prof_stop) {
       cudaError_t e = cudaEventRecordWithFlags(g_prof_start, st, cudaEventRecordExternal);
       if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
     }
-    int rc = launch_project_plan(t->key_dtype, b->x_dtype, a, a.qtiles * a.nsplit, proj_smem_bytes(t->l), st);
+    int rc = launch_project(t->key_dtype, b->x_dtype, a, st);
     if (rc) return rc;
     DecodeScanArgs d{};
     d.s.keys = keys;
@@ -339,8 +395,9 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     }
     return ALUT_OK;
   }
-  const size_t smem1 = std::max(proj_smem_bytes(t->l), plan_smem_bytes(2 * t->num_experts));
-  int rc = launch_project_plan(t->key_dtype, b->x_dtype, a, a.qtiles * a.nsplit + 1, smem1, st);
+  int rc = launch_plan(a, st);
+  if (rc) return rc;
+  rc = launch_project(t->key_dtype, b->x_dtype, a, st);
   if (rc) return rc;
 
   SearchArgs s{};
@@ -403,6 +460,12 @@ extern "C" {
 
 int alut_version(void) { return 100; }
 
+#ifdef ALUT_PHASE_TRACE
+int alut_debug_trace(unsigned long long* host, int n) {
+  return cudaMemcpyFromSymbol(host, g_alut_trace, sizeof(unsigned long long) * (n < 64 ? n : 64)) == cudaSuccess ? 0 : -4;
+}
+#endif
+
 int alut_set_profile_events(void* start_event, void* stop_event) {
   if ((start_event == nullptr) != (stop_event == nullptr))
     return fail(ALUT_EINVAL, "profile events must be both set or both NULL");
@@ -450,14 +513,10 @@ int alut_project(const alut_tables_t* tables, const alut_batch_t* batch, int32_t
   a.nsplit = proj_splits(batch->q, tables->h);
   a.normalize = normalize_q;
   a.eps = eps;
-  a.qpart = reinterpret_cast<float*>(base + w.qpart);
   a.qlow = reinterpret_cast<float*>(base + w.qlow);
-  a.counters = reinterpret_cast<uint32_t*>(base + w.counters);
   a.q_out = q_low;
   a.q_out_stride = q_low_stride;
-  a.do_plan = 0;
-  return launch_project_plan(tables->key_dtype, batch->x_dtype, a, a.qtiles * a.nsplit,
-                             proj_smem_bytes(tables->l), reinterpret_cast<cudaStream_t>(stream));
+  return launch_project(tables->key_dtype, batch->x_dtype, a, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int alut_search(const alut_tables_t* tables, const alut_batch_t* batch,

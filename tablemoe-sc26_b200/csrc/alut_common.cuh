@@ -110,6 +110,23 @@ template <typename T> __device__ __forceinline__ void load8_rw(const T* p, float
   for (int i = 0; i < 8; ++i) o[i] = to_f32<T>(p[i]);
 }
 
+// ---- optional phase trace (development builds with -DALUT_PHASE_TRACE only) -----------
+#ifdef ALUT_PHASE_TRACE
+__device__ unsigned long long g_alut_trace[64];
+#define ALUT_TRACE(slot)                                                              \
+  do {                                                                                \
+    if (threadIdx.x == 0 && blockIdx.x == 0) {                                        \
+      unsigned long long t_;                                                          \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                          \
+      g_alut_trace[slot] = t_;                                                        \
+    }                                                                                 \
+  } while (0)
+#else
+#define ALUT_TRACE(slot) \
+  do {                   \
+  } while (0)
+#endif
+
 // ---- cp.async (16-byte global -> shared copies, waited per commit group) -----------------
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
@@ -174,15 +191,12 @@ __device__ __forceinline__ bool hit_rule(float score, float thr, int cmp_ge) {
 // ---- workspace layout ---------------------------------------------------------------
 // All offsets are multiples of 256 bytes from the workspace base.
 struct Workspace {
-  size_t counters;  // uint32 [qtiles]       projection split arrival counters (self-resetting)
   size_t meta;      // int32  [8]            [0] search groups, [1] error bits
-  size_t qpart;     // f32    [rows * L]     projection split partial sums
   size_t qlow;      // f32    [Q * L]        projected queries (already rounded to key dtype)
   size_t best;      // uint64 [Q * S]        packed best candidate per slot
   size_t sorted;    // int32  [Q * S]        slot ids sorted by table
   size_t groups;    // int4   [max_groups]   (table, first sorted slot, count, 0)
   size_t total;
-  int64_t qpart_rows;
   int64_t max_groups;
 };
 
@@ -190,35 +204,27 @@ __host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~size_
 
 inline int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
-// Number of H splits of the projection for q tokens (more splits when few tokens, so
-// that a decode batch still spreads over the whole GPU).
+// Number of H splits of the projection for q tokens: a power of two <= kMaxClusterSplit
+// (the split CTAs form one thread-block cluster) when the batch is small, so that a decode
+// batch still spreads its projection over several SMs; 1 for large batches.
+constexpr int kMaxClusterSplit = 16;  // a non-portable cluster size, allowed on sm_100
 inline int proj_splits(int q, int h) {
-  int qtiles = ceil_div(q, kProjTileQ);
-  // At least 2 basis chunks (128 rows of H) per split, so that the split partials stay few
-  // and the chunk pipeline has something to overlap.
-  int max_split = ceil_div(h, 2 * kProjChunkH);
-  if (max_split > 64) max_split = 64;
-  if (max_split < 1) max_split = 1;
-  int s = kProjSplitTarget / (qtiles > 0 ? qtiles : 1);
-  if (s < 1) s = 1;
-  if (s > max_split) s = max_split;
+  const int qtiles = ceil_div(q, kProjTileQ);
+  int cap = kProjSplitTarget / (qtiles > 0 ? qtiles : 1);
+  const int by_h = ceil_div(h, kProjChunkH);  // >= 1 chunk per split
+  if (cap > by_h) cap = by_h;
+  if (cap > kMaxClusterSplit) cap = kMaxClusterSplit;
+  int s = 1;
+  while (s * 2 <= cap) s *= 2;
   return s;
 }
 
 inline Workspace workspace_layout(int q, int s, int l, int num_tables) {
   Workspace w{};
-  int qtiles = ceil_div(q, kProjTileQ);
-  int64_t pairs = static_cast<int64_t>(q) * s;
-  int64_t rows = static_cast<int64_t>(qtiles > kProjSplitTarget ? qtiles : kProjSplitTarget) *
-                 kProjTileQ;
-  // proj_splits(q') * ceil(q'/16) <= max(kProjSplitTarget, ceil(q/16)) for every q' <= q.
-  w.qpart_rows = rows;
-  w.max_groups = (pairs + kSearchGroup - 1) / kSearchGroup +
-                 (pairs < num_tables ? pairs : num_tables) + 1;
+  const int64_t pairs = static_cast<int64_t>(q) * s;
+  w.max_groups = (pairs + kSearchGroup - 1) / kSearchGroup + (pairs < num_tables ? pairs : num_tables) + 1;
   size_t off = 0;
-  w.counters = off; off = align256(off + sizeof(uint32_t) * (qtiles + 1));
   w.meta = off;     off = align256(off + sizeof(int32_t) * 8);
-  w.qpart = off;    off = align256(off + sizeof(float) * rows * l);
   w.qlow = off;     off = align256(off + sizeof(float) * (static_cast<int64_t>(q) * l + 8));
   w.best = off;     off = align256(off + sizeof(uint64_t) * (pairs + 1));
   w.sorted = off;   off = align256(off + sizeof(int32_t) * (pairs + 1));

@@ -1,12 +1,23 @@
-// Kernel 1 of the search: PCA projection of the queries (search.py:476-498) fused with
-// the planning step that buckets the searched (token, slot) pairs by (expert, modality)
-// table, so that the search kernel streams every table once for all pairs routed to it
-// (the reference's Triton kernel re-reads the table once per pair, search.py:80-84).
+// Kernel 1 of the search: PCA projection of the queries (search.py:476-498), plus the
+// planning kernel that buckets the searched (token, slot) pairs by (expert, modality)
+// table for large batches, so that the scan streams every table once for all pairs routed
+// to it (the reference's Triton kernel re-reads the table once per pair, search.py:80-84).
+//
+// Projection: a CTA computes a 16-token x L tile over a range of H. Basis rows and token
+// chunks stream through two shared-memory buffers with cp.async; each thread owns one
+// column l and NOUT tokens, so one basis element feeds NOUT FMAs. When H is split over
+// several CTAs (small batches), those CTAs form a thread-block cluster and add their
+// partial tiles through distributed shared memory in split order - no global partials,
+// atomics or fences, and the same sum on every run.
 #pragma once
+
+#include <cooperative_groups.h>
 
 #include "alut_common.cuh"
 
 namespace alut {
+
+namespace cg = cooperative_groups;
 
 struct ProjPlanArgs {
   // projection
@@ -19,13 +30,13 @@ struct ProjPlanArgs {
   const void* q_in;  // optional precomputed query [Q,L] in the key dtype
   int q, h, l, nsplit, qtiles, normalize;
   float eps;
-  float* qpart;
   float* qlow;
-  uint32_t* counters;
   void* q_out;  // optional typed copy of the query (alut_project)
   int64_t q_out_stride;
+  // decode path: clear best[0, zero_n) for the scan that follows
+  uint64_t* zero_best;
+  int zero_n;
   // plan
-  int do_plan;
   int s;
   int num_experts;
   const int64_t* sel;
@@ -36,28 +47,35 @@ struct ProjPlanArgs {
   int* sorted;
   int4* groups;
   int* meta;
-  // decode path: zero best[0, zero_n) (no planning CTA)
-  uint64_t* zero_best;
-  int zero_n;
 };
 
-constexpr int kProjOutPerThread = (kProjTileQ * kMaxL) / kProjThreads;  // 16
+// Tokens per thread (a thread owns one column l of NOUT tokens; 16/NOUT token groups of L
+// threads fit in the CTA): 4 for L <= 64, 8 for L <= 128, 16 for L <= 256.
+inline int proj_nout(int l) { return l <= 64 ? 4 : (l <= 128 ? 8 : 16); }
 
-// Dynamic shared memory of one projection CTA: two pipeline buffers, each holding both
-// modalities' basis chunk [kProjChunkH][L] and the token chunk [kProjTileQ][kProjChunkH] in
-// their storage dtypes (<= 4 bytes); the area is reused for the fp32 output tile.
-// Basis rows per pipeline chunk: 64, or 32 when L > 128 so two buffers fit in 227 KB.
-__host__ __device__ inline int proj_chunk_rows(int l) { return l > 128 ? kProjChunkH / 2 : kProjChunkH; }
-__host__ __device__ inline size_t proj_buffer_bytes(int l) {
+// Basis rows per pipeline chunk: 64, or 32 when L > 128 so that everything fits in 227 KB.
+__host__ __device__ inline int proj_chunk_rows(int l) { return l > 128 ? 32 : 64; }
+
+// Shared memory: two pipeline buffers (both modalities' basis chunk [HC][L] and the raw
+// token chunk [16][HC], each in its storage dtype of <= 4 bytes), the fp32 token chunk
+// transposed [HC][16], and two fp32 [16][L] tiles (this CTA's partial, the reduced rows).
+struct ProjSmem {
+  size_t buf, xt, tile, red, total;
+};
+__host__ __device__ inline ProjSmem proj_smem_layout(int l) {
   const int hc = proj_chunk_rows(l);
-  return align256(sizeof(float) * (2 * hc * l + kProjTileQ * hc));
+  ProjSmem s;
+  s.buf = align256(sizeof(float) * (2 * hc * l + kProjTileQ * hc));
+  s.xt = 2 * s.buf;
+  s.tile = s.xt + align256(sizeof(float) * hc * kProjTileQ);
+  s.red = s.tile + align256(sizeof(float) * kProjTileQ * l);
+  s.total = s.red + align256(sizeof(float) * kProjTileQ * l);
+  return s;
 }
-inline size_t proj_smem_bytes(int l) {
-  size_t a = 2 * proj_buffer_bytes(l);
-  size_t tile = sizeof(float) * kProjTileQ * l;
-  return a > tile ? a : tile;
-}
+inline size_t proj_smem_bytes(int l) { return proj_smem_layout(l).total; }
 inline size_t plan_smem_bytes(int num_tables) { return sizeof(int) * 3 * num_tables; }
+
+// ---- planning (large batches) --------------------------------------------------------------
 
 __device__ __forceinline__ int block_exclusive_scan_256(int v, int* scratch, int* total) {
   // Hillis-Steele inclusive scan over 256 threads, returned as exclusive.
@@ -76,14 +94,15 @@ __device__ __forceinline__ int block_exclusive_scan_256(int v, int* scratch, int
   return incl - v;
 }
 
-// Bucket the searched pairs by table. Runs in one CTA of kProjThreads threads.
-__device__ void plan_pairs(const ProjPlanArgs& a, int* smem) {
+// Bucket the searched pairs by table (one CTA of kProjThreads threads): per-table counts,
+// block scans, group list (<= kSearchGroup pairs of one table each), scatter of pair ids.
+__global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
+  extern __shared__ __align__(16) int plan_smem[];
   const int tid = threadIdx.x;
   const int ntab = 2 * a.num_experts;
   const int64_t pairs = static_cast<int64_t>(a.q) * a.s;
-  int* counts = smem;
-  int* offs = smem + ntab;
-  int* gofs = smem + 2 * ntab;
+  int* counts = plan_smem;
+  int* offs = plan_smem + ntab;
   __shared__ int scan_scratch[kProjThreads];
   __shared__ int s_tot_c, s_tot_g;
 
@@ -100,11 +119,9 @@ __device__ void plan_pairs(const ProjPlanArgs& a, int* smem) {
       atomicOr(&a.meta[1], 1);
       continue;
     }
-    const int t = static_cast<int>(e) * 2 + (a.is_vision[qq] ? 0 : 1);
-    atomicAdd(&counts[t], 1);
+    atomicAdd(&counts[static_cast<int>(e) * 2 + (a.is_vision[qq] ? 0 : 1)], 1);
   }
   __syncthreads();
-  // Exclusive scans of the pair counts and of the group counts per table.
   const int per = (ntab + kProjThreads - 1) / kProjThreads;
   const int t0 = tid * per;
   const int t1 = min(ntab, t0 + per);
@@ -117,11 +134,9 @@ __device__ void plan_pairs(const ProjPlanArgs& a, int* smem) {
   int bg = block_exclusive_scan_256(lg, scan_scratch, &s_tot_g);
   for (int t = t0; t < t1; ++t) {
     offs[t] = bc;
-    gofs[t] = bg;
     const int c = counts[t];
-    for (int g = 0; g * kSearchGroup < c; ++g) {
+    for (int g = 0; g * kSearchGroup < c; ++g)
       a.groups[bg + g] = make_int4(t, bc + g * kSearchGroup, min(kSearchGroup, c - g * kSearchGroup), 0);
-    }
     bc += c;
     bg += (c + kSearchGroup - 1) / kSearchGroup;
   }
@@ -135,27 +150,24 @@ __device__ void plan_pairs(const ProjPlanArgs& a, int* smem) {
     if (!r) continue;
     const int64_t e = a.sel[qq * a.sel_stride + ss];
     if (e < 0 || e >= a.num_experts) continue;
-    const int t = static_cast<int>(e) * 2 + (a.is_vision[qq] ? 0 : 1);
-    const int pos = atomicAdd(&offs[t], 1);
+    const int pos = atomicAdd(&offs[static_cast<int>(e) * 2 + (a.is_vision[qq] ? 0 : 1)], 1);
     a.sorted[pos] = static_cast<int>(p);
   }
 }
 
-// Bias, rounding to the key dtype and optional L2 normalisation of one finished tile
-// held in shared memory (search.py:12-21, :484-488). One warp per row.
+// ---- projection ---------------------------------------------------------------------------
+
+// Bias, rounding to the key dtype and optional L2 normalisation of rows [r0, r1) of a
+// finished tile (search.py:12-21, :484-488). One warp per row.
 template <typename TP, typename TK>
-__device__ void finish_tile(const ProjPlanArgs& a, float* tile, int q0, int nq,
-                            const int* mod, bool add_bias) {
+__device__ void finish_rows(const ProjPlanArgs& a, float* tile, int q0, int r0, int r1, const int* mod) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L = a.l;
-  for (int r = warp; r < nq; r += kProjThreads / 32) {
-    const int m = mod[r];
-    const TP* b = static_cast<const TP*>(a.bias[m]);
+  for (int r = r0 + warp; r < r1; r += kProjThreads / 32) {
+    const TP* b = static_cast<const TP*>(a.bias[mod[r]]);
     float ss = 0.f;
     for (int c = lane; c < L; c += 32) {
-      float v = tile[r * L + c];
-      if (add_bias) v = v + to_f32<TP>(b[c]);
-      v = round_as<TK>(v);
+      const float v = round_as<TK>(tile[r * L + c] + to_f32<TP>(b[c]));
       tile[r * L + c] = v;
       ss = fmaf(v, v, ss);
     }
@@ -179,26 +191,25 @@ __device__ void finish_tile(const ProjPlanArgs& a, float* tile, int q0, int nq,
   }
 }
 
-template <typename TX, typename TP, typename TK>
-__global__ void __launch_bounds__(kProjThreads) k_project_plan(ProjPlanArgs a) {
-  extern __shared__ __align__(256) float smem[];
+template <typename TX, typename TP, typename TK, int NOUT>
+__global__ void __launch_bounds__(kProjThreads) k_project(ProjPlanArgs a) {
+  extern __shared__ __align__(256) unsigned char psm[];
+  ALUT_TRACE(0);
   pdl_launch_dependents();
   if (a.zero_best && blockIdx.x == 0)
     for (int i = threadIdx.x; i < a.zero_n; i += kProjThreads) a.zero_best[i] = 0ull;
-  const int nproj = a.qtiles * a.nsplit;
-  if (a.do_plan && static_cast<int>(blockIdx.x) == nproj) {
-    plan_pairs(a, reinterpret_cast<int*>(smem));
-    return;
-  }
   const int tid = threadIdx.x;
   const int L = a.l;
   const int qt = blockIdx.x / a.nsplit;
-  const int sp = blockIdx.x % a.nsplit;
+  const int sp = blockIdx.x % a.nsplit;  // == rank in the cluster when nsplit > 1
   const int q0 = qt * kProjTileQ;
   const int nq = min(kProjTileQ, a.q - q0);
+  const ProjSmem lay = proj_smem_layout(L);
+  float* tile = reinterpret_cast<float*>(psm + lay.tile);
+  float* red = reinterpret_cast<float*>(psm + lay.red);
+  float* xt = reinterpret_cast<float*>(psm + lay.xt);
   __shared__ int mod[kProjTileQ];
   __shared__ int need[2];
-  __shared__ int s_last;
   if (tid < 2) need[tid] = 0;
   __syncthreads();
   if (tid < kProjTileQ) {
@@ -207,48 +218,46 @@ __global__ void __launch_bounds__(kProjThreads) k_project_plan(ProjPlanArgs a) {
     if (tid < nq) need[m] = 1;
   }
   __syncthreads();
+  ALUT_TRACE(1);
 
-  float* tile = smem;
   if (a.q_in) {
-    // Precomputed query: copy it (already in the key dtype) and skip the projection.
+    // Precomputed query (already in the key dtype): copy it, no projection (nsplit == 1).
     const TK* qi = static_cast<const TK*>(a.q_in);
     for (int i = tid; i < nq * L; i += kProjThreads) {
-      const int r = i / L, c = i % L;
-      const float v = to_f32<TK>(qi[static_cast<int64_t>(q0 + r) * L + c]);
-      a.qlow[static_cast<int64_t>(q0 + r) * L + c] = v;
-      if (a.q_out) static_cast<TK*>(a.q_out)[static_cast<int64_t>(q0 + r) * a.q_out_stride + c] = qi[static_cast<int64_t>(q0 + r) * L + c];
+      const int64_t o = static_cast<int64_t>(q0) * L + i;
+      a.qlow[o] = to_f32<TK>(qi[o]);
+      if (a.q_out) static_cast<TK*>(a.q_out)[(q0 + i / L) * a.q_out_stride + i % L] = qi[o];
     }
     return;
   }
 
-  // Basis and token chunks stream through two shared-memory buffers with cp.async
-  // (16-byte copies when rows are 16-byte multiples and aligned, else 4-byte ones or plain
-  // loads), so the next chunk is in flight while this one is multiplied.
-  const int nout = (kProjTileQ * L + kProjThreads - 1) / kProjThreads;
-  float acc[kProjOutPerThread];
-  int oq[kProjOutPerThread], ol[kProjOutPerThread];
+  // Thread -> (column l, token group g): tokens g*NOUT .. g*NOUT+NOUT-1.
+  constexpr int kGroups = kProjTileQ / NOUT;
+  const int l = tid % L;
+  const int g = tid / L;
+  const bool active = g < kGroups;
+  float acc[NOUT];
 #pragma unroll
-  for (int i = 0; i < kProjOutPerThread; ++i) {
-    acc[i] = 0.f;
-    const int o = tid + i * kProjThreads;
-    oq[i] = o / L;
-    ol[i] = o % L;
-  }
+  for (int i = 0; i < NOUT; ++i) acc[i] = 0.f;
+  int mbits = 0;  // bit i: token g*NOUT+i is a text token
+  if (active)
+#pragma unroll
+    for (int i = 0; i < NOUT; ++i) mbits |= mod[g * NOUT + i] << i;
+
   const int HC = proj_chunk_rows(L);
   const int nch = (a.h + HC - 1) / HC;
   const int c_begin = static_cast<int>(static_cast<int64_t>(sp) * nch / a.nsplit);
   const int c_end = static_cast<int>(static_cast<int64_t>(sp + 1) * nch / a.nsplit);
   const TX* x = static_cast<const TX*>(a.x);
-  const size_t buf_bytes = proj_buffer_bytes(L);
   const bool p_vec = (L * sizeof(TP)) % 16 == 0 && (a.proj_stride * sizeof(TP)) % 16 == 0 &&
                      (reinterpret_cast<uintptr_t>(a.proj[0]) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(a.proj[1]) & 15) == 0;
   const bool x_vec = (HC * sizeof(TX)) % 16 == 0 && (a.x_stride * sizeof(TX)) % 16 == 0 &&
-                     (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.h * sizeof(TX)) % 16 == 0;
+                     (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
   auto stage = [&](int c, int b) {
-    unsigned char* base = reinterpret_cast<unsigned char*>(smem) + b * buf_bytes;
-    TP* ps = reinterpret_cast<TP*>(base);                                   // [2][HC][L]
-    TX* xs = reinterpret_cast<TX*>(base + sizeof(float) * 2 * HC * L);  // [16][HC]
+    unsigned char* base = psm + b * lay.buf;
+    TP* ps = reinterpret_cast<TP*>(base);                                 // [2][HC][L]
+    TX* xs = reinterpret_cast<TX*>(base + sizeof(float) * 2 * HC * L);    // [16][HC]
     const int h0 = c * HC;
     const int hn = min(HC, a.h - h0);
 #pragma unroll
@@ -276,9 +285,11 @@ __global__ void __launch_bounds__(kProjThreads) k_project_plan(ProjPlanArgs a) {
       const int per_row = HC / kE;
       for (int i = tid; i < kProjTileQ * per_row; i += kProjThreads) {
         const int r = i / per_row, u = i % per_row;
-        if (r < nq) cp_async16(xs + r * HC + u * kE, x + static_cast<int64_t>(q0 + r) * a.x_stride + h0 + u * kE);
-        else
+        if (r < nq) {
+          cp_async16(xs + r * HC + u * kE, x + static_cast<int64_t>(q0 + r) * a.x_stride + h0 + u * kE);
+        } else {
           for (int e = 0; e < kE; ++e) xs[r * HC + u * kE + e] = TX(0.f);
+        }
       }
     } else {
       for (int i = tid; i < kProjTileQ * HC; i += kProjThreads) {
@@ -288,7 +299,9 @@ __global__ void __launch_bounds__(kProjThreads) k_project_plan(ProjPlanArgs a) {
     }
     cp_async_commit();
   };
+
   if (c_begin < c_end) stage(c_begin, 0);
+  ALUT_TRACE(2);
   for (int c = c_begin; c < c_end; ++c) {
     const int b = (c - c_begin) & 1;
     if (c + 1 < c_end) {
@@ -298,58 +311,83 @@ __global__ void __launch_bounds__(kProjThreads) k_project_plan(ProjPlanArgs a) {
       cp_async_wait<0>();
     }
     __syncthreads();
-    const unsigned char* base = reinterpret_cast<const unsigned char*>(smem) + b * buf_bytes;
+    if (c == c_begin) ALUT_TRACE(3);
+    const unsigned char* base = psm + b * lay.buf;
     const TP* ps = reinterpret_cast<const TP*>(base);
     const TX* xs = reinterpret_cast<const TX*>(base + sizeof(float) * 2 * HC * L);
+    // Tokens to fp32, transposed to [HC][16] so a thread reads its NOUT tokens with 16-byte loads.
+    for (int i = tid; i < kProjTileQ * HC; i += kProjThreads) {
+      const int r = i / HC, hh = i % HC;
+      xt[hh * kProjTileQ + r] = to_f32<TX>(xs[i]);
+    }
+    __syncthreads();
+    if (active && !(need[0] && need[1])) {
+      // One modality in the tile (the common case): no per-token select.
+      const TP* pb = ps + (need[0] ? 0 : HC * L) + l;
+#pragma unroll 4
+      for (int hh = 0; hh < HC; ++hh) {
+        const float bw = to_f32<TP>(pb[hh * L]);
+        const float* xr = xt + hh * kProjTileQ + g * NOUT;
 #pragma unroll
-    for (int i = 0; i < kProjOutPerThread; ++i) {
-      if (i < nout && oq[i] < kProjTileQ) {
-        const TP* prow = ps + mod[oq[i]] * HC * L + ol[i];
-        const TX* xrow = xs + oq[i] * HC;
-        float v = acc[i];
-#pragma unroll 16
-        for (int hh = 0; hh < HC; ++hh) v = fmaf(to_f32<TX>(xrow[hh]), to_f32<TP>(prow[hh * L]), v);
-        acc[i] = v;
+        for (int i = 0; i < NOUT; i += 4) {
+          const float4 xv = *reinterpret_cast<const float4*>(xr + i);
+          acc[i + 0] = fmaf(xv.x, bw, acc[i + 0]);
+          acc[i + 1] = fmaf(xv.y, bw, acc[i + 1]);
+          acc[i + 2] = fmaf(xv.z, bw, acc[i + 2]);
+          acc[i + 3] = fmaf(xv.w, bw, acc[i + 3]);
+        }
+      }
+    } else if (active) {
+      const TP* pv = ps + l;
+      const TP* pt = ps + HC * L + l;
+      const bool nv = need[0], nt = need[1];
+#pragma unroll 4
+      for (int hh = 0; hh < HC; ++hh) {
+        const float bv = nv ? to_f32<TP>(pv[hh * L]) : 0.f;
+        const float bt = nt ? to_f32<TP>(pt[hh * L]) : 0.f;
+        const float* xr = xt + hh * kProjTileQ + g * NOUT;
+#pragma unroll
+        for (int i = 0; i < NOUT; i += 4) {
+          const float4 xv = *reinterpret_cast<const float4*>(xr + i);
+          acc[i + 0] = fmaf(xv.x, (mbits >> (i + 0)) & 1 ? bt : bv, acc[i + 0]);
+          acc[i + 1] = fmaf(xv.y, (mbits >> (i + 1)) & 1 ? bt : bv, acc[i + 1]);
+          acc[i + 2] = fmaf(xv.z, (mbits >> (i + 2)) & 1 ? bt : bv, acc[i + 2]);
+          acc[i + 3] = fmaf(xv.w, (mbits >> (i + 3)) & 1 ? bt : bv, acc[i + 3]);
+        }
       }
     }
-    __syncthreads();  // buffer b may be refilled by the next iteration's stage()
+    __syncthreads();  // buffer b and xt may be refilled
+    if (c == c_begin) ALUT_TRACE(4);
   }
+  ALUT_TRACE(5);
+  if (active)
+#pragma unroll
+    for (int i = 0; i < NOUT; ++i) tile[(g * NOUT + i) * L + l] = acc[i];
+
   if (a.nsplit == 1) {
-#pragma unroll
-    for (int i = 0; i < kProjOutPerThread; ++i)
-      if (i < nout && oq[i] < kProjTileQ) tile[oq[i] * L + ol[i]] = acc[i];
-  } else {
-    float* part = a.qpart + static_cast<int64_t>(qt * a.nsplit + sp) * kProjTileQ * L;
-#pragma unroll
-    for (int i = 0; i < kProjOutPerThread; ++i)
-      if (i < nout && oq[i] < kProjTileQ) __stcg(part + oq[i] * L + ol[i], acc[i]);
-    __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&a.counters[qt], 1u) == static_cast<unsigned>(a.nsplit - 1));
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    if (tid == 0) a.counters[qt] = 0u;
-    // The last CTA of the tile sums the partials in split order (deterministic).
-    const float* base = a.qpart + static_cast<int64_t>(qt * a.nsplit) * kProjTileQ * L;
-    // Loads are issued 8 splits at a time (independent), then added in split order.
-    const int64_t stride = static_cast<int64_t>(kProjTileQ) * L;
-    for (int i = tid; i < kProjTileQ * L; i += kProjThreads) {
-      float v = 0.f;
-      int k = 0;
-      for (; k + 8 <= a.nsplit; k += 8) {
-        float p[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) p[u] = __ldcg(base + (k + u) * stride + i);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) v += p[u];
-      }
-      for (; k < a.nsplit; ++k) v += __ldcg(base + k * stride + i);
-      tile[i] = v;
-    }
+    finish_rows<TP, TK>(a, tile, q0, 0, nq, mod);
+    return;
+  }
+  // Split over a cluster: rank sp reduces rows [r0, r1) over all ranks' partial tiles, in
+  // rank order, then finishes them.
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  ALUT_TRACE(6);
+  const int rows_per = (kProjTileQ + a.nsplit - 1) / a.nsplit;
+  const int r0 = min(nq, sp * rows_per);
+  const int r1 = min(nq, r0 + rows_per);
+  for (int i = r0 * L + tid; i < r1 * L; i += kProjThreads) {
+    float v = 0.f;
+    for (int k = 0; k < a.nsplit; ++k) v += cluster.map_shared_rank(tile, k)[i];
+    red[i] = v;
   }
   __syncthreads();
-  finish_tile<TP, TK>(a, tile, q0, nq, mod, true);
+  ALUT_TRACE(7);
+  finish_rows<TP, TK>(a, red, q0, r0, r1, mod);
+  ALUT_TRACE(8);
+  cluster.sync();
+  ALUT_TRACE(9);  // peers may still be reading this CTA's tile
 }
 
 }  // namespace alut
