@@ -191,6 +191,25 @@ int alut_merge_packed(int32_t world, int32_t q, int32_t s, const uint64_t* packe
                       const uint8_t* is_vision, const alut_search_params_t* params,
                       uint8_t* out_hit, int64_t* out_idx, alut_stream_t stream);
 
+/* alut_lookup_combine for callers that cannot allocate device memory: those handed only
+ * their input and output buffers by another runtime (an FFI host without access to the
+ * CUDA allocator, a serving loop that forbids cudaMalloc after start-up because it can
+ * synchronise the device). It has no counterpart in the reference. Its scratch is a
+ * fixed 2 MiB array inside this library (held by every GPU that loads the library until
+ * the process exits); batches whose scratch would exceed it (alut_workspace_size() >
+ * ALUT_NOALLOC_SCRATCH_BYTES) are rejected with ALUT_ERANGE. The first call on a device
+ * looks up the array's device address (make it before any stream capture). All calls on
+ * a device share the array: calls that may overlap on the GPU (different streams without
+ * ordering between them) race and give wrong results. It calls no cudaMalloc/cudaFree. */
+#define ALUT_NOALLOC_SCRATCH_BYTES (2u << 20)
+int alut_lookup_combine_noalloc(const alut_tables_t* tables, const alut_batch_t* batch,
+                                const alut_search_params_t* params, const float* weights,
+                                int64_t weight_stride, const uint8_t* compute_mask,
+                                int64_t compute_stride, int32_t renorm, int32_t accumulate,
+                                void* out, int64_t out_stride, int32_t out_dtype,
+                                uint8_t* out_hit, int64_t* out_idx, int64_t out_stride_hit,
+                                alut_stream_t stream);
+
 /* Profiling hook: when both events are set (cudaEvent_t handles), every following
  * centroid-scan launch made by this thread is bracketed by event records on its stream
  * (as external event nodes when the stream is being captured into a CUDA graph), so the

@@ -746,3 +746,62 @@ int alut_merge_packed(int32_t world, int32_t q, int32_t s, const uint64_t* packe
 }
 
 }  // extern "C"
+
+// ---- no-allocation variant of alut_lookup_combine ------------------------------------------
+// The scratch of alut_lookup_combine_noalloc: one fixed array per device, shared by all its
+// calls. Host code must not pass the symbol itself to a kernel (on the host it only names a
+// stand-in); its device address comes from cudaGetSymbolAddress, looked up once per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[ALUT_NOALLOC_SCRATCH_BYTES];
+
+namespace alut {
+static void* noalloc_scratch_ptr(int* rc) {
+  static void* ptrs[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *rc = fail(ALUT_ECUDA, "noalloc: no usable current device (%s)", cudaGetErrorString(e));
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      *rc = fail(ALUT_ECUDA, "noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  *rc = ALUT_OK;
+  return ptrs[dev];
+}
+}  // namespace alut
+
+extern "C" int alut_lookup_combine_noalloc(const alut_tables_t* tables, const alut_batch_t* batch,
+                                           const alut_search_params_t* params, const float* weights,
+                                           int64_t weight_stride, const uint8_t* compute_mask,
+                                           int64_t compute_stride, int32_t renorm, int32_t accumulate,
+                                           void* out, int64_t out_stride, int32_t out_dtype,
+                                           uint8_t* out_hit, int64_t* out_idx, int64_t out_stride_hit,
+                                           alut_stream_t stream) {
+  if (!tables || !batch) return fail(ALUT_EINVAL, "tables/batch is NULL");
+  if (batch->q < 0 || batch->s < 0 || tables->l <= 0 || tables->num_experts <= 0)
+    return fail(ALUT_EINVAL, "noalloc: bad sizes");
+  const size_t need = workspace_layout(batch->q, batch->s, tables->l, 2 * tables->num_experts).total;
+  if (need > ALUT_NOALLOC_SCRATCH_BYTES)
+    return fail(ALUT_ERANGE, "noalloc: batch needs %zu bytes of scratch, the fixed array holds %u", need,
+                ALUT_NOALLOC_SCRATCH_BYTES);
+  int rc = ALUT_OK;
+  void* scratch = noalloc_scratch_ptr(&rc);
+  if (!scratch) return rc;
+  // The meta words (group count, error bits) start from zero on every call; everything
+  // else in the scratch is written before it is read.
+  const Workspace w = workspace_layout(batch->q, batch->s, tables->l, 2 * tables->num_experts);
+  cudaError_t e = cudaMemsetAsync(static_cast<char*>(scratch) + w.meta, 0, sizeof(int32_t) * 8,
+                                  reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "noalloc: clearing scratch: %s", cudaGetErrorString(e));
+  return alut_lookup_combine(tables, batch, params, weights, weight_stride, compute_mask, compute_stride, renorm,
+                             accumulate, out, out_stride, out_dtype, out_hit, out_idx, out_stride_hit, scratch,
+                             ALUT_NOALLOC_SCRATCH_BYTES, stream);
+}

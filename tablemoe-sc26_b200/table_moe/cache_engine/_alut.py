@@ -22,6 +22,7 @@ ALUT_OK = 0
 ALUT_EINVAL, ALUT_EDTYPE, ALUT_ESHAPE, ALUT_ECUDA, ALUT_EWORKSPACE, ALUT_ERANGE = -1, -2, -3, -4, -5, -6
 KEYS_NORMALISED, KEYS_RAW = 0, 1
 RENORM_NONE, RENORM_TO_ONE, RENORM_TO_ROWSUM = 0, 1, 2
+NOALLOC_SCRATCH_BYTES = 2 << 20  # ALUT_NOALLOC_SCRATCH_BYTES
 
 _DTYPE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
@@ -72,6 +73,8 @@ SIGNATURES = {
                                     _I64, _I32, _P]),
     "alut_lookup_combine": (ctypes.c_int, [_TP, _BP, _PP, _P, _I64, _P, _I64, _I32, _I32, _P, _I64,
                                            _I32, _P, _P, _I64, _P, _SZ, _P]),
+    "alut_lookup_combine_noalloc": (ctypes.c_int, [_TP, _BP, _PP, _P, _I64, _P, _I64, _I32, _I32, _P, _I64,
+                                                   _I32, _P, _P, _I64, _P]),
     "alut_search_packed": (ctypes.c_int, [_TP, _BP, _PP, _P, _I64, _P, _P, _SZ, _P]),
     "alut_merge_packed": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _PP, _P, _P, _P]),
     "alut_set_profile_events": (ctypes.c_int, [_P, _P]),
