@@ -97,6 +97,10 @@ typedef struct alut_tables {
   int64_t key_stride[3];   /* strides of dims e, m, k (keys and raw_keys share them) */
   int64_t value_stride[3]; /* strides of dims e, m, k */
   int64_t proj_stride_h;   /* row stride of proj */
+  /* Optional: the fp32 basis split into three bf16 parts, [2 modalities][3][L][H]
+   * (hi + mid + lo == proj to fp32 precision), written by alut_prepare_basis. When set and
+   * x is bf16, small batches project on tensor cores; NULL keeps the CUDA-core path. */
+  const void* proj_split;
 } alut_tables_t;
 
 /* One batch of routed tokens. */
@@ -129,6 +133,14 @@ typedef struct alut_search_params {
 /* Bytes of workspace needed for batches of up to q tokens x s slots on these tables.
  * Returns 0 on invalid arguments. */
 size_t alut_workspace_size(const alut_tables_t* tables, int32_t q, int32_t s);
+
+/* Bytes of the split basis of these tables (0 if the tables do not qualify: fp32 proj,
+ * H % 16 == 0, L % 8 == 0). */
+size_t alut_basis_split_bytes(const alut_tables_t* tables);
+
+/* Write the split basis (see alut_tables_t.proj_split) of tables->proj into out, a device
+ * buffer of alut_basis_split_bytes() bytes. Once per table load; the basis is static. */
+int alut_prepare_basis(const alut_tables_t* tables, void* out, size_t out_bytes, alut_stream_t stream);
 
 /* a1: q_low[Q,L] = x[mask_m] @ proj_m + bias_m per modality, optionally L2-normalised,
  * written in the key dtype (search.py:476-498). */

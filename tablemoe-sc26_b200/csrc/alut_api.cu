@@ -145,18 +145,16 @@ static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 
 // Projection: grid = qtiles x nsplit CTAs; the nsplit CTAs of a token tile form one
 // thread-block cluster (they add their partial tiles through distributed shared memory).
-template <typename TX, typename TK>
-static int launch_project_t(const ProjPlanArgs& args, size_t smem, cudaStream_t st) {
+static int launch_project_kernel(void (*kern)(ProjPlanArgs), const ProjPlanArgs& args, size_t smem,
+                                 cudaStream_t st) {
   ProjPlanArgs a = args;
-  const int nout = proj_nout(a.l);
-  auto kern = nout == 4 ? k_project<TX, TK, TK, 4> : (nout == 8 ? k_project<TX, TK, TK, 8> : k_project<TX, TK, TK, 16>);
   int rc = allow_smem(reinterpret_cast<const void*>(kern), smem);
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(kProjThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
@@ -200,9 +198,21 @@ static int launch_project_t(const ProjPlanArgs& args, size_t smem, cudaStream_t 
   }
   cfg.gridDim = dim3(a.qtiles * a.nsplit);
   attr[0].val.clusterDim.x = a.nsplit;
+  // Programmatic dependent of whatever precedes it in the stream: the kernel prefetches
+  // its static tables, then waits (griddepcontrol.wait) before reading any input.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
   if (e != cudaSuccess) return fail(ALUT_ECUDA, "k_project: %s", cudaGetErrorString(e));
   return check_launch("k_project");
+}
+
+template <typename TX, typename TK>
+static int launch_project_t(const ProjPlanArgs& a, size_t smem, cudaStream_t st) {
+  const int nout = proj_nout(a.l);
+  auto kern = nout == 4 ? k_project<TX, TK, TK, 4> : (nout == 8 ? k_project<TX, TK, TK, 8> : k_project<TX, TK, TK, 16>);
+  return launch_project_kernel(kern, a, smem, st);
 }
 
 template <typename TK>
@@ -215,8 +225,16 @@ static int launch_project_k(int x_dtype, const ProjPlanArgs& a, size_t smem, cud
   return fail(ALUT_EDTYPE, "x dtype");
 }
 
+// Whether the tensor-core projection applies: split basis present, bf16 tokens with 4-byte
+// aligned rows, fp32 basis and keys, H % 16 == 0, L % 8 == 0.
+static bool mma_projection_ok(int key_dtype, int x_dtype, const ProjPlanArgs& a) {
+  return a.proj_split != nullptr && x_dtype == ALUT_BF16 && key_dtype == ALUT_F32 && a.h % 16 == 0 &&
+         a.l % 8 == 0 && (reinterpret_cast<uintptr_t>(a.x) & 3) == 0 && a.x_stride % 2 == 0 && a.q_in == nullptr;
+}
+
 static int launch_project(int key_dtype, int x_dtype, const ProjPlanArgs& a, cudaStream_t st) {
   const size_t smem = proj_smem_bytes(a.l);
+  if (mma_projection_ok(key_dtype, x_dtype, a)) return launch_project_kernel(k_project_mma<float>, a, smem, st);
   switch (key_dtype) {
     case ALUT_F32: return launch_project_k<float>(x_dtype, a, smem, st);
     case ALUT_BF16: return launch_project_k<__nv_bfloat16>(x_dtype, a, smem, st);
@@ -332,6 +350,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     a.bias[m] = t->bias[m];
   }
   a.proj_stride = t->proj_stride_h;
+  a.proj_split = static_cast<const __nv_bfloat16*>(t->proj_split);
   a.q_in = q_low_in;
   a.q = b->q;
   a.h = t->h;
@@ -476,6 +495,22 @@ int alut_set_profile_events(void* start_event, void* stop_event) {
 
 const char* alut_last_error(void) { return g_err; }
 
+size_t alut_basis_split_bytes(const alut_tables_t* t) {
+  if (!t || t->proj_dtype != ALUT_F32 || t->h <= 0 || t->l <= 0 || t->h % 16 != 0 || t->l % 8 != 0) return 0;
+  return static_cast<size_t>(2) * 3 * t->l * t->h * sizeof(__nv_bfloat16);
+}
+
+int alut_prepare_basis(const alut_tables_t* t, void* out, size_t out_bytes, alut_stream_t stream) {
+  const size_t need = alut_basis_split_bytes(t);
+  if (need == 0) return fail(ALUT_EINVAL, "prepare_basis: tables do not qualify (fp32 proj, h%%16, l%%8)");
+  if (!out || out_bytes < need) return fail(ALUT_EINVAL, "prepare_basis: out needs %zu bytes", need);
+  if (!t->proj[0] || !t->proj[1] || t->proj_stride_h < t->l) return fail(ALUT_EINVAL, "prepare_basis: proj");
+  k_split_basis<<<592, kProjThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const float*>(t->proj[0]), static_cast<const float*>(t->proj[1]), t->proj_stride_h, t->h, t->l,
+      static_cast<__nv_bfloat16*>(out));
+  return check_launch("k_split_basis");
+}
+
 size_t alut_workspace_size(const alut_tables_t* tables, int32_t q, int32_t s) {
   if (!tables || q < 0 || s < 0 || tables->l <= 0 || tables->num_experts <= 0) return 0;
   return workspace_layout(q, s, tables->l, 2 * tables->num_experts).total;
@@ -506,6 +541,7 @@ int alut_project(const alut_tables_t* tables, const alut_batch_t* batch, int32_t
     a.bias[m] = tables->bias[m];
   }
   a.proj_stride = tables->proj_stride_h;
+  a.proj_split = static_cast<const __nv_bfloat16*>(tables->proj_split);
   a.q = batch->q;
   a.h = tables->h;
   a.l = tables->l;

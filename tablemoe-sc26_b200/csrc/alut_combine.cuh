@@ -52,6 +52,7 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
   __shared__ int s_n;
   const int tid = threadIdx.x;
   const int t = blockIdx.x;
+  ALUT_TRACE(20);
   pdl_launch_dependents();
   // Inputs first (they do not depend on the search), then wait for the search results.
   bool r_ = false, ev_ = false, comp_ = false;
@@ -65,7 +66,9 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
     comp_ = a.compute ? (a.compute[t * a.compute_stride + tid] != 0) : false;
     w_ = a.w[t * a.w_stride + tid];
   }
+  ALUT_TRACE(21);
   pdl_wait();
+  ALUT_TRACE(22);
   for (int s = tid; s < a.s; s += kCombineThreads) {
     const bool r = r_;
     const int64_t e = e_;
@@ -115,6 +118,7 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
     s_n = n;
   }
   __syncthreads();
+  ALUT_TRACE(23);
   if (!a.out) return;
   const int n = s_n;
   const int64_t h0 = static_cast<int64_t>(blockIdx.y) * kCombineSpan + tid * 8;
@@ -136,6 +140,7 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
       for (int j = 0; j < 8; ++j) acc[j] = fmaf(w, v[j], acc[j]);
     }
     store8<TO>(out, acc);
+    ALUT_TRACE(24);
   } else {
     const int64_t rem = a.h - h0;
     const int cnt = rem < 8 ? static_cast<int>(rem) : 8;

@@ -115,13 +115,20 @@ template <typename T> __device__ __forceinline__ void load8_rw(const T* p, float
 __device__ unsigned long long g_alut_trace[64];
 #define ALUT_TRACE(slot)                                                              \
   do {                                                                                \
-    if (threadIdx.x == 0 && blockIdx.x == 0) {                                        \
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) {                     \
       unsigned long long t_;                                                          \
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                          \
       g_alut_trace[slot] = t_;                                                        \
     }                                                                                 \
   } while (0)
+#define ALUT_TRACE_VAL(slot, v)                                                      \
+  do {                                                                               \
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) g_alut_trace[slot] = (v); \
+  } while (0)
 #else
+#define ALUT_TRACE_VAL(slot, v) \
+  do {                          \
+  } while (0)
 #define ALUT_TRACE(slot) \
   do {                   \
   } while (0)

@@ -47,6 +47,8 @@ struct ProjPlanArgs {
   int* sorted;
   int4* groups;
   int* meta;
+  // tensor-core projection: bf16 split basis [2][3][L][H] (see alut_prepare_basis)
+  const __nv_bfloat16* proj_split;
 };
 
 // Tokens per thread (a thread owns one column l of NOUT tokens; 16/NOUT token groups of L
@@ -159,15 +161,16 @@ __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
 
 // Bias, rounding to the key dtype and optional L2 normalisation of rows [r0, r1) of a
 // finished tile (search.py:12-21, :484-488). One warp per row.
-template <typename TP, typename TK>
-__device__ void finish_rows(const ProjPlanArgs& a, float* tile, int q0, int r0, int r1, const int* mod) {
+template <typename TK>
+__device__ void finish_rows(const ProjPlanArgs& a, float* tile, int q0, int r0, int r1, const int* mod,
+                            const float (*bias)[kMaxL]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L = a.l;
   for (int r = r0 + warp; r < r1; r += kProjThreads / 32) {
-    const TP* b = static_cast<const TP*>(a.bias[mod[r]]);
+    const float* b = bias[mod[r]];
     float ss = 0.f;
     for (int c = lane; c < L; c += 32) {
-      const float v = round_as<TK>(tile[r * L + c] + to_f32<TP>(b[c]));
+      const float v = round_as<TK>(tile[r * L + c] + b[c]);
       tile[r * L + c] = v;
       ss = fmaf(v, v, ss);
     }
@@ -196,8 +199,6 @@ __global__ void __launch_bounds__(kProjThreads) k_project(ProjPlanArgs a) {
   extern __shared__ __align__(256) unsigned char psm[];
   ALUT_TRACE(0);
   pdl_launch_dependents();
-  if (a.zero_best && blockIdx.x == 0)
-    for (int i = threadIdx.x; i < a.zero_n; i += kProjThreads) a.zero_best[i] = 0ull;
   const int tid = threadIdx.x;
   const int L = a.l;
   const int qt = blockIdx.x / a.nsplit;
@@ -210,6 +211,52 @@ __global__ void __launch_bounds__(kProjThreads) k_project(ProjPlanArgs a) {
   float* xt = reinterpret_cast<float*>(psm + lay.xt);
   __shared__ int mod[kProjTileQ];
   __shared__ int need[2];
+  __shared__ float s_bias[2][kMaxL];
+  // Before waiting for the previous kernel: only static tables are read (the first basis
+  // chunk of both modalities and the biases), so this overlaps the predecessor's tail when
+  // the kernel is launched as a programmatic dependent.
+  // proj_chunk_rows(L) as a constant: NOUT 16 <=> L > 128 <=> 32 rows, else 64.
+  constexpr int HC = NOUT == 16 ? 32 : 64;
+  const int nch = (a.h + HC - 1) / HC;
+  const int c_begin = static_cast<int>(static_cast<int64_t>(sp) * nch / a.nsplit);
+  const int c_end = static_cast<int>(static_cast<int64_t>(sp + 1) * nch / a.nsplit);
+  const bool p_vec = (L * sizeof(TP)) % 16 == 0 && (a.proj_stride * sizeof(TP)) % 16 == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.proj[0]) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.proj[1]) & 15) == 0;
+  auto stage_p = [&](int c, int b, int mask) {
+    TP* ps = reinterpret_cast<TP*>(psm + b * lay.buf);  // [2][HC][L]
+    const int h0 = c * HC;
+    const int hn = min(HC, a.h - h0);
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      if (!((mask >> m) & 1)) continue;
+      const TP* pg = static_cast<const TP*>(a.proj[m]) + static_cast<int64_t>(h0) * a.proj_stride;
+      TP* pd = ps + m * HC * L;
+      if (p_vec) {
+        constexpr int kE = 16 / sizeof(TP);
+        const int per_row = L / kE;
+        for (int i = tid; i < hn * per_row; i += kProjThreads) {
+          const int r = i / per_row, u = i % per_row;
+          cp_async16(pd + r * L + u * kE, pg + static_cast<int64_t>(r) * a.proj_stride + u * kE);
+        }
+      } else {
+        for (int i = tid; i < hn * L; i += kProjThreads) {
+          const int r = i / L, col = i % L;
+          pd[r * L + col] = pg[static_cast<int64_t>(r) * a.proj_stride + col];
+        }
+      }
+      for (int i = hn * L + tid; i < HC * L; i += kProjThreads) pd[i] = TP(0.f);
+    }
+  };
+  if (!a.q_in) {
+    if (c_begin < c_end) stage_p(c_begin, 0, 3);
+    cp_async_commit();
+    for (int i = tid; i < 2 * L; i += kProjThreads)
+      s_bias[i / L][i % L] = to_f32<TP>(static_cast<const TP*>(a.bias[i / L])[i % L]);
+  }
+  pdl_wait();
+  if (a.zero_best && blockIdx.x == 0)
+    for (int i = tid; i < a.zero_n; i += kProjThreads) a.zero_best[i] = 0ull;
   if (tid < 2) need[tid] = 0;
   __syncthreads();
   if (tid < kProjTileQ) {
@@ -244,42 +291,16 @@ __global__ void __launch_bounds__(kProjThreads) k_project(ProjPlanArgs a) {
 #pragma unroll
     for (int i = 0; i < NOUT; ++i) mbits |= mod[g * NOUT + i] << i;
 
-  const int HC = proj_chunk_rows(L);
-  const int nch = (a.h + HC - 1) / HC;
-  const int c_begin = static_cast<int>(static_cast<int64_t>(sp) * nch / a.nsplit);
-  const int c_end = static_cast<int>(static_cast<int64_t>(sp + 1) * nch / a.nsplit);
   const TX* x = static_cast<const TX*>(a.x);
-  const bool p_vec = (L * sizeof(TP)) % 16 == 0 && (a.proj_stride * sizeof(TP)) % 16 == 0 &&
-                     (reinterpret_cast<uintptr_t>(a.proj[0]) & 15) == 0 &&
-                     (reinterpret_cast<uintptr_t>(a.proj[1]) & 15) == 0;
   const bool x_vec = (HC * sizeof(TX)) % 16 == 0 && (a.x_stride * sizeof(TX)) % 16 == 0 &&
                      (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
-  auto stage = [&](int c, int b) {
+  // Token chunk (and, after the first chunk, the needed modalities' basis chunk).
+  auto stage = [&](int c, int b, bool with_p) {
     unsigned char* base = psm + b * lay.buf;
-    TP* ps = reinterpret_cast<TP*>(base);                                 // [2][HC][L]
     TX* xs = reinterpret_cast<TX*>(base + sizeof(float) * 2 * HC * L);    // [16][HC]
     const int h0 = c * HC;
     const int hn = min(HC, a.h - h0);
-#pragma unroll
-    for (int m = 0; m < 2; ++m) {
-      if (!need[m]) continue;
-      const TP* pg = static_cast<const TP*>(a.proj[m]) + static_cast<int64_t>(h0) * a.proj_stride;
-      TP* pd = ps + m * HC * L;
-      if (p_vec) {
-        constexpr int kE = 16 / sizeof(TP);
-        const int per_row = L / kE;
-        for (int i = tid; i < hn * per_row; i += kProjThreads) {
-          const int r = i / per_row, u = i % per_row;
-          cp_async16(pd + r * L + u * kE, pg + static_cast<int64_t>(r) * a.proj_stride + u * kE);
-        }
-      } else {
-        for (int i = tid; i < hn * L; i += kProjThreads) {
-          const int r = i / L, col = i % L;
-          pd[r * L + col] = pg[static_cast<int64_t>(r) * a.proj_stride + col];
-        }
-      }
-      for (int i = hn * L + tid; i < HC * L; i += kProjThreads) pd[i] = TP(0.f);
-    }
+    if (with_p) stage_p(c, b, need[0] | (need[1] << 1));
     if (x_vec && hn == HC) {
       constexpr int kE = 16 / sizeof(TX);
       const int per_row = HC / kE;
@@ -300,12 +321,12 @@ __global__ void __launch_bounds__(kProjThreads) k_project(ProjPlanArgs a) {
     cp_async_commit();
   };
 
-  if (c_begin < c_end) stage(c_begin, 0);
+  if (c_begin < c_end) stage(c_begin, 0, false);
   ALUT_TRACE(2);
   for (int c = c_begin; c < c_end; ++c) {
     const int b = (c - c_begin) & 1;
     if (c + 1 < c_end) {
-      stage(c + 1, b ^ 1);
+      stage(c + 1, b ^ 1, true);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
@@ -316,15 +337,24 @@ __global__ void __launch_bounds__(kProjThreads) k_project(ProjPlanArgs a) {
     const TP* ps = reinterpret_cast<const TP*>(base);
     const TX* xs = reinterpret_cast<const TX*>(base + sizeof(float) * 2 * HC * L);
     // Tokens to fp32, transposed to [HC][16] so a thread reads its NOUT tokens with 16-byte loads.
+#ifdef ALUT_PHASE_TRACE
+    const long long ck0 = clock64();
+#endif
     for (int i = tid; i < kProjTileQ * HC; i += kProjThreads) {
       const int r = i / HC, hh = i % HC;
       xt[hh * kProjTileQ + r] = to_f32<TX>(xs[i]);
     }
+#ifdef ALUT_PHASE_TRACE
+    const long long ck1 = clock64();
+#endif
     __syncthreads();
+#ifdef ALUT_PHASE_TRACE
+    const long long ck2 = clock64();
+#endif
     if (active && !(need[0] && need[1])) {
       // One modality in the tile (the common case): no per-token select.
       const TP* pb = ps + (need[0] ? 0 : HC * L) + l;
-#pragma unroll 4
+#pragma unroll 16
       for (int hh = 0; hh < HC; ++hh) {
         const float bw = to_f32<TP>(pb[hh * L]);
         const float* xr = xt + hh * kProjTileQ + g * NOUT;
@@ -356,6 +386,14 @@ __global__ void __launch_bounds__(kProjThreads) k_project(ProjPlanArgs a) {
         }
       }
     }
+#ifdef ALUT_PHASE_TRACE
+    const long long ck3 = clock64();
+    if (c == c_begin) {
+      ALUT_TRACE_VAL(33, ck1 - ck0);
+      ALUT_TRACE_VAL(34, ck2 - ck1);
+      ALUT_TRACE_VAL(35, ck3 - ck2);
+    }
+#endif
     __syncthreads();  // buffer b and xt may be refilled
     if (c == c_begin) ALUT_TRACE(4);
   }
@@ -366,7 +404,7 @@ __global__ void __launch_bounds__(kProjThreads) k_project(ProjPlanArgs a) {
 
   if (a.nsplit == 1) {
     __syncthreads();
-    finish_rows<TP, TK>(a, tile, q0, 0, nq, mod);
+    finish_rows<TK>(a, tile, q0, 0, nq, mod, s_bias);
     return;
   }
   // Split over a cluster: rank sp reduces rows [r0, r1) over all ranks' partial tiles, in
@@ -384,10 +422,175 @@ __global__ void __launch_bounds__(kProjThreads) k_project(ProjPlanArgs a) {
   }
   __syncthreads();
   ALUT_TRACE(7);
-  finish_rows<TP, TK>(a, red, q0, r0, r1, mod);
+  finish_rows<TK>(a, red, q0, r0, r1, mod, s_bias);
   ALUT_TRACE(8);
   cluster.sync();
   ALUT_TRACE(9);  // peers may still be reading this CTA's tile
+}
+
+// ---- tensor-core projection (small batches, bf16 tokens, fp32 basis) ----------------------
+// q = x @ P with x exact in bf16 and P = hi + mid + lo split into three bf16 parts (the
+// split is exact to fp32 precision), so mma.sync m16n8k16 (bf16 in, fp32 accumulate) over
+// the three parts gives an fp32-accurate product. One m16 tile is the 16-token tile; warp w
+// owns the 8-column n-tiles w, w+8, ...; a CTA covers a range of k-steps (16 rows of H) and
+// the split CTAs of a token tile reduce through distributed shared memory as in k_project.
+// The split basis is static, so the first block of it is requested before griddepcontrol.wait.
+
+__global__ void __launch_bounds__(kProjThreads) k_split_basis(const float* proj0, const float* proj1,
+                                                            int64_t stride_h, int h, int l,
+                                                            __nv_bfloat16* out) {
+  const int64_t n = static_cast<int64_t>(2) * l * h;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(i / (static_cast<int64_t>(l) * h));
+    const int64_t r = i % (static_cast<int64_t>(l) * h);
+    const int col = static_cast<int>(r / h), k = static_cast<int>(r % h);
+    const float p = (m == 0 ? proj0 : proj1)[static_cast<int64_t>(k) * stride_h + col];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(p);
+    const float r1 = p - __bfloat162float(hi);
+    const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+    const int64_t plane = static_cast<int64_t>(l) * h;
+    __nv_bfloat16* o = out + static_cast<int64_t>(m) * 3 * plane + static_cast<int64_t>(col) * h + k;
+    o[0] = hi;
+    o[plane] = mid;
+    o[2 * plane] = lo;
+  }
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+constexpr int kMmaKBlock = 8;  // k-steps (x 16 rows of H) whose fragments are loaded together
+
+template <typename TK>
+__global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
+  extern __shared__ __align__(256) unsigned char psm[];
+  ALUT_TRACE(0);
+  pdl_launch_dependents();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;  // mma fragment row group / thread-in-group
+  const int L = a.l, H = a.h;
+  const int qt = blockIdx.x / a.nsplit;
+  const int sp = blockIdx.x % a.nsplit;
+  const int q0 = qt * kProjTileQ;
+  const int nq = min(kProjTileQ, a.q - q0);
+  const ProjSmem lay = proj_smem_layout(L);
+  float* tile = reinterpret_cast<float*>(psm + lay.tile);
+  float* red = reinterpret_cast<float*>(psm + lay.red);
+  __shared__ int mod[kProjTileQ];
+  __shared__ int need[2];
+  __shared__ float s_bias[2][kMaxL];
+  const int ksteps = H / 16;
+  const int k_begin = static_cast<int>(static_cast<int64_t>(sp) * ksteps / a.nsplit);
+  const int k_end = static_cast<int>(static_cast<int64_t>(sp + 1) * ksteps / a.nsplit);
+  const int ntiles = L / 8;
+  const int64_t plane = static_cast<int64_t>(L) * H;
+  const uint32_t* ps32 = reinterpret_cast<const uint32_t*>(a.proj_split);
+  // Static data first: biases, and an L2 prefetch of this CTA's slice of the split basis.
+  for (int i = tid; i < 2 * L; i += kProjThreads)
+    s_bias[i / L][i % L] = static_cast<const float*>(a.bias[i / L])[i % L];
+  {
+    const int rows = 2 * 3 * L;  // (modality, part, column) rows of H elements
+    const int64_t kb = static_cast<int64_t>(k_begin) * 16, kn = static_cast<int64_t>(k_end - k_begin) * 16;
+    for (int r = tid; r < rows; r += kProjThreads) {
+      const char* base = reinterpret_cast<const char*>(a.proj_split + static_cast<int64_t>(r) * H + kb);
+      for (int64_t off = 0; off < kn * 2; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
+    }
+  }
+  pdl_wait();
+  if (a.zero_best && blockIdx.x == 0)
+    for (int i = tid; i < a.zero_n; i += kProjThreads) a.zero_best[i] = 0ull;
+  if (tid < 2) need[tid] = 0;
+  __syncthreads();
+  if (tid < kProjTileQ) {
+    const int m = tid < nq ? (a.is_vision[q0 + tid] ? 0 : 1) : 1;
+    mod[tid] = m;
+    if (tid < nq) need[m] = 1;
+  }
+  __syncthreads();
+  ALUT_TRACE(1);
+  const bool row0_ok = gq < nq, row1_ok = gq + 8 < nq;
+  const int m_r0 = mod[gq], m_r1 = mod[gq + 8];
+  const __nv_bfloat16* xr0 = static_cast<const __nv_bfloat16*>(a.x) + static_cast<int64_t>(q0 + (row0_ok ? gq : 0)) * a.x_stride;
+  const __nv_bfloat16* xr1 = static_cast<const __nv_bfloat16*>(a.x) + static_cast<int64_t>(q0 + (row1_ok ? gq + 8 : 0)) * a.x_stride;
+  for (int nt = warp; nt < ntiles; nt += kProjThreads / 32) {
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int kb = k_begin; kb < k_end; kb += kMmaKBlock) {
+      const int kn = min(kMmaKBlock, k_end - kb);
+      uint32_t xa[kMmaKBlock][4];
+#pragma unroll
+      for (int s = 0; s < kMmaKBlock; ++s) {
+        if (s < kn) {
+          const int k0 = (kb + s) * 16 + 2 * tq;
+          xa[s][0] = row0_ok ? *reinterpret_cast<const uint32_t*>(xr0 + k0) : 0u;
+          xa[s][1] = row1_ok ? *reinterpret_cast<const uint32_t*>(xr1 + k0) : 0u;
+          xa[s][2] = row0_ok ? *reinterpret_cast<const uint32_t*>(xr0 + k0 + 8) : 0u;
+          xa[s][3] = row1_ok ? *reinterpret_cast<const uint32_t*>(xr1 + k0 + 8) : 0u;
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        if (!need[m]) continue;
+        // Rows of the other modality are zeroed in A, so the two passes add exactly.
+        const uint32_t keep0 = (m_r0 == m) ? 0xffffffffu : 0u, keep1 = (m_r1 == m) ? 0xffffffffu : 0u;
+        const uint32_t* bcol = ps32 + (static_cast<int64_t>(m) * 3 * plane + static_cast<int64_t>(nt * 8 + gq) * H) / 2;
+        uint32_t bf[kMmaKBlock][3][2];
+#pragma unroll
+        for (int s = 0; s < kMmaKBlock; ++s) {
+          if (s < kn) {
+            const int64_t k0 = static_cast<int64_t>(kb + s) * 16 + 2 * tq;
+#pragma unroll
+            for (int part = 0; part < 3; ++part) {
+              bf[s][part][0] = bcol[(part * plane + k0) / 2];
+              bf[s][part][1] = bcol[(part * plane + k0 + 8) / 2];
+            }
+          }
+        }
+#pragma unroll
+        for (int s = 0; s < kMmaKBlock; ++s) {
+          if (s < kn) {
+            const uint32_t am[4] = {xa[s][0] & keep0, xa[s][1] & keep1, xa[s][2] & keep0, xa[s][3] & keep1};
+#pragma unroll
+            for (int part = 0; part < 3; ++part) mma_bf16_16816(c, am, bf[s][part][0], bf[s][part][1]);
+          }
+        }
+      }
+    }
+    const int col = nt * 8 + 2 * tq;
+    tile[gq * L + col] = c[0];
+    tile[gq * L + col + 1] = c[1];
+    tile[(gq + 8) * L + col] = c[2];
+    tile[(gq + 8) * L + col + 1] = c[3];
+  }
+  ALUT_TRACE(5);
+  if (a.nsplit == 1) {
+    __syncthreads();
+    finish_rows<TK>(a, tile, q0, 0, nq, mod, s_bias);
+    return;
+  }
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  ALUT_TRACE(6);
+  const int rows_per = (kProjTileQ + a.nsplit - 1) / a.nsplit;
+  const int r0 = min(nq, sp * rows_per);
+  const int r1 = min(nq, r0 + rows_per);
+  for (int i = r0 * L + tid; i < r1 * L; i += kProjThreads) {
+    float v = 0.f;
+    for (int k = 0; k < a.nsplit; ++k) v += cluster.map_shared_rank(tile, k)[i];
+    red[i] = v;
+  }
+  __syncthreads();
+  ALUT_TRACE(7);
+  finish_rows<TK>(a, red, q0, r0, r1, mod, s_bias);
+  ALUT_TRACE(8);
+  cluster.sync();
+  ALUT_TRACE(9);
 }
 
 }  // namespace alut

@@ -178,6 +178,50 @@ __device__ __forceinline__ void score_row(const TK* row, bool valid, const float
   }
 }
 
+// score_row with L fixed at compile time (the common ranks): the row's 16-byte units are
+// all loaded from shared memory first, then every slot's dot product runs on registers.
+template <typename TK, int LC>
+__device__ __forceinline__ void score_row_fixed(const TK* row, bool valid, const float* qs, int cnt, int kbase,
+                                                float (*red_s)[kSearchGroup], int (*red_k)[kSearchGroup]) {
+  constexpr int kEpu = 16 / sizeof(TK);
+  constexpr int kUnits = LC / kEpu;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float kv[LC];
+  if (valid) {
+#pragma unroll
+    for (int u = 0; u < kUnits; ++u) {
+      float t[8];
+      unit_to_f32<TK>(row + u * kEpu, t);
+#pragma unroll
+      for (int e = 0; e < kEpu; ++e) kv[u * kEpu + e] = t[e];
+    }
+  }
+  for (int j = 0; j < cnt; ++j) {
+    const float4* q4 = reinterpret_cast<const float4*>(qs + j * LC);
+    float a0 = 0.f, a1 = 0.f;  // two partial chains; summed as (a0 + a1) in a fixed order
+    if (valid) {
+#pragma unroll
+      for (int c = 0; c < LC / 4; ++c) {
+        const float4 q = q4[c];
+        float& a = (c < LC / 8) ? a0 : a1;
+        a = fmaf(kv[4 * c + 0], q.x, a);
+        a = fmaf(kv[4 * c + 1], q.y, a);
+        a = fmaf(kv[4 * c + 2], q.z, a);
+        a = fmaf(kv[4 * c + 3], q.w, a);
+      }
+    }
+    const float sc = valid ? round_as<TK>(a0 + a1) : -INFINITY;
+    float m = sc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const unsigned bal = __ballot_sync(0xffffffffu, valid && sc == m);
+    if (lane == 0) {
+      red_s[warp][j] = m;
+      red_k[warp][j] = bal ? kbase + warp * 32 + __ffs(bal) - 1 : -1;
+    }
+  }
+}
+
 // After a __syncthreads: thread j < cnt merges the warps' candidates of slot j and folds
 // the result into best[pid[j]].
 __device__ __forceinline__ void fold_slots(int cnt, const int* pid, uint32_t idx_offset, uint64_t* best,
@@ -346,6 +390,7 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
   const int pairs = d.q * a.s;
   const int p = blockIdx.x;
   const int chunk = blockIdx.y;
+  ALUT_TRACE(10);
   pdl_launch_dependents();
 
   // Table of every slot of the batch (-1: not searched or bad expert id).
@@ -392,8 +437,10 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
     bulk_g2s(kbuf + static_cast<size_t>(tid) * pitch, src, row_bytes, &bar[0]);
   }
   const int cnt = s_cnt;
+  ALUT_TRACE(11);
   // The queries (and the cleared best buffer) come from the projection kernel.
   pdl_wait();
+  ALUT_TRACE(12);
   for (int i = tid; i < cnt * L; i += kSearchThreads) {
     const int j = i / L, c = i % L;
     qs[i] = a.qlow[static_cast<int64_t>(pid[j] / a.s) * L + c];
@@ -407,11 +454,31 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
     if (tid == 0) mbar_wait_bounded(&bar[0], 0);
     return;
   }
+  ALUT_TRACE(13);
   const bool ok = mbar_try_wait(&bar[0], 0);
   const TK* row = reinterpret_cast<const TK*>(kbuf + static_cast<size_t>(tid) * pitch);
-  score_row<TK, true>(row, ok && tid < rows, qs, L, cnt, chunk * kSearchChunkK, red_s, red_k);
+#ifdef ALUT_PHASE_TRACE
+  {
+    const long long c0 = clock64();
+    if (L == 64) score_row_fixed<TK, 64>(row, ok && tid < rows, qs, cnt, chunk * kSearchChunkK, red_s, red_k);
+    const long long c1 = clock64();
+    ALUT_TRACE_VAL(30, c1 - c0);
+    ALUT_TRACE_VAL(31, cnt);
+    ALUT_TRACE_VAL(32, rows);
+  }
   __syncthreads();
+  ALUT_TRACE(16);
+#endif
+  if (L == 64)
+    score_row_fixed<TK, 64>(row, ok && tid < rows, qs, cnt, chunk * kSearchChunkK, red_s, red_k);
+  else if (L == 128)
+    score_row_fixed<TK, 128>(row, ok && tid < rows, qs, cnt, chunk * kSearchChunkK, red_s, red_k);
+  else
+    score_row<TK, true>(row, ok && tid < rows, qs, L, cnt, chunk * kSearchChunkK, red_s, red_k);
+  __syncthreads();
+  ALUT_TRACE(14);
   fold_slots(cnt, pid, a.idx_offset, a.best, red_s, red_k);
+  ALUT_TRACE(15);
 }
 
 // ---- packed best -> (hit, idx) (search.py:597-602 / :689-697) -------------------------------

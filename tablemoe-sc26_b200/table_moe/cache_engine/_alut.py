@@ -35,7 +35,7 @@ class Tables(ctypes.Structure):
         ("keys", ctypes.c_void_p), ("raw_keys", ctypes.c_void_p), ("values", ctypes.c_void_p),
         ("proj", ctypes.c_void_p * 2), ("bias", ctypes.c_void_p * 2),
         ("key_stride", ctypes.c_int64 * 3), ("value_stride", ctypes.c_int64 * 3),
-        ("proj_stride_h", ctypes.c_int64),
+        ("proj_stride_h", ctypes.c_int64), ("proj_split", ctypes.c_void_p),
     ]
 
 
@@ -66,6 +66,8 @@ _PP = ctypes.POINTER(SearchParams)
 
 SIGNATURES = {
     "alut_workspace_size": (_SZ, [_TP, _I32, _I32]),
+    "alut_basis_split_bytes": (_SZ, [_TP]),
+    "alut_prepare_basis": (ctypes.c_int, [_TP, _P, _SZ, _P]),
     "alut_project": (ctypes.c_int, [_TP, _BP, _I32, ctypes.c_float, _P, _I64, _P, _SZ, _P]),
     "alut_search": (ctypes.c_int, [_TP, _BP, _PP, _P, _P, _P, _I64, _P, _SZ, _P]),
     "alut_gather_rows": (ctypes.c_int, [_TP, _I32, _P, _P, _P, _P, _P, _I64, _P]),
@@ -138,9 +140,10 @@ def _inner_contig(t: torch.Tensor, name: str) -> None:
         raise ValueError(f"{name} must have unit innermost stride")
 
 
-def make_tables(keys, raw_keys, values, proj_vis, bias_vis, proj_txt, bias_txt) -> Tables:
+def make_tables(keys, raw_keys, values, proj_vis, bias_vis, proj_txt, bias_txt, proj_split=None) -> Tables:
     """Describe one layer's tables. keys/raw_keys: [E,2,K,L]; values: [E,2,K,H];
-    proj: [H,L]; bias: [L]. keys, raw_keys or values may be None."""
+    proj: [H,L]; bias: [L]. keys, raw_keys or values may be None. proj_split: the bf16
+    split basis written by alut_prepare_basis (optional)."""
     ref = keys if keys is not None else raw_keys
     if ref is None:
         raise ValueError("keys and raw_keys cannot both be None")
@@ -187,10 +190,26 @@ def make_tables(keys, raw_keys, values, proj_vis, bias_vis, proj_txt, bias_txt) 
         t.h = proj_vis.shape[0]
     else:
         t.proj_dtype = t.key_dtype
+    if proj_split is not None:
+        t.proj_split = proj_split.data_ptr()
     return t
 
 
+def prepare_basis(tables: Tables, device):
+    """The tensor-core split of an fp32 basis (a static [2,3,L,H] bf16 tensor), or None when
+    the tables do not qualify. Made once per table load."""
+    lib = load()
+    n = int(lib.alut_basis_split_bytes(tables))
+    if n == 0:
+        return None
+    out = torch.empty(n // 2, dtype=torch.bfloat16, device=device)
+    check(lib.alut_prepare_basis(tables, out.data_ptr(), n, stream_ptr(device)), "alut_prepare_basis")
+    return out
+
+
 def make_batch(x, sel, is_vision, reuse) -> Batch:
+    """Describe one batch. The struct holds raw device pointers only: the caller keeps the
+    tensors alive (and unmodified) until the work using them has been issued and run."""
     b = Batch()
     Q, S = sel.shape
     b.q, b.s = Q, S

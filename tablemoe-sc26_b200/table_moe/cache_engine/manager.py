@@ -115,6 +115,10 @@ class HybridStorageManager:
         if self._tables is None or self._tables[0] != key:
             t = _alut.make_tables(self.keys_buffer, self.raw_keys_buffer, self.values_buffer,
                                   pv["proj"], pv["bias"], pt["proj"], pt["bias"])
+            # Static tensor-core split of an fp32 basis (used for bf16 tokens, small batches).
+            self._proj_split = _alut.prepare_basis(t, self.device) if self.device.type == "cuda" else None
+            if self._proj_split is not None:
+                t.proj_split = self._proj_split.data_ptr()
             self._tables = (key, t)
         return self._tables[1]
 

@@ -292,10 +292,15 @@ class VectorSearchEngine:
             if comp is not None and (comp.dtype != torch.bool or comp.stride(-1) != 1):
                 comp = comp.bool().contiguous()
             sel = selected_experts if selected_experts.dtype == torch.int64 else selected_experts.long()
+            sel = sel if sel.stride(-1) == 1 else sel.contiguous()
             vis = is_vision_mask.reshape(-1).bool().contiguous()
+            x = hidden_states if hidden_states.stride(-1) == 1 else hidden_states.contiguous()
+            reuse = reuse_mask
+            if reuse is not None and (reuse.dtype != torch.bool or reuse.stride(-1) != 1):
+                reuse = reuse.bool().contiguous()
             tables = self._tables(with_values=True)
             ws = self._scratch(tables, bs, top_k)
-            batch = _alut.make_batch(hidden_states, sel.contiguous(), vis, reuse_mask)
+            batch = _alut.make_batch(x, sel, vis, reuse)  # x, sel, vis, reuse stay referenced
             params = _alut.make_params(keyset, normalize, cmp_ge, tv, tt, CacheConfig.OFFLINE_COSINE_EPS)
             rc = self._lib.alut_lookup_combine(
                 tables, batch, params, w.data_ptr(), w.stride(0), _alut.ptr(comp),

@@ -145,9 +145,34 @@ def oracle_dot(s, dtype="float32"):
 
 
 def gpu_dot(mgr, s, dtype=torch.float32):
+    """dtype: the dtype the tokens are handed over in (bf16 tokens with fp32 tables take the
+    tensor-core projection for small batches)."""
     eng = VectorSearchEngine(mgr)
     return eng.search_prefill_offline_dot(0, s["x"].to(dtype).to(DEV), s["sel"].to(DEV), s["vis"].to(DEV),
                                           s["reuse"].to(DEV))
+
+
+@pytest.mark.parametrize("Q,vis_frac,H,L", [(16, 0.0, 2048, 64), (16, 0.5, 2048, 64), (37, 0.5, 1024, 96),
+                                            (300, 0.3, 512, 128), (5, 1.0, 256, 8)])
+def test_tensor_core_projection_matches_oracle(Q, vis_frac, H, L):
+    """bf16 tokens + fp32 basis: q from the three-part bf16 split on tensor cores."""
+    s = synth(Q=Q, S=4, E=12, K=300, L=L, H=H, seed=Q + L, vis_frac=vis_frac, reuse_p=0.6)
+    mgr = synth_manager(s)
+    assert mgr.alut_tables().proj_split
+    hit, idx = gpu_dot(mgr, s, dtype=torch.bfloat16)
+    q, keys, rh, ri = oracle_dot(s)
+    check_search(hit.cpu().numpy(), idx.cpu().numpy(), rh, ri, q, keys, s["sel"].numpy(), s["vis"].numpy(),
+                 (0.0, 0.0), "float32", what=f"mma Q{Q}")
+    lib = _alut.load()
+    t = mgr.alut_tables()
+    xb, selb, visb = s["x"].to(DEV), s["sel"].to(DEV), s["vis"].to(DEV)  # alive during the call
+    b = _alut.make_batch(xb, selb, visb, None)
+    ws = torch.zeros(lib.alut_workspace_size(t, Q, 4), dtype=torch.uint8, device=DEV)
+    qg = torch.empty(Q, L, device=DEV)
+    _alut.check(lib.alut_project(t, ctypes.byref(b), 0, 1e-6, qg.data_ptr(), L, ws.data_ptr(), ws.numel(),
+                                 _alut.stream_ptr(DEV)), "alut_project")
+    bound = np.abs(s["x"].float().numpy()).sum(axis=1, keepdims=True) * float(np.abs(s["proj"].numpy()).max())
+    assert np.all(np.abs(qg.cpu().numpy() - q) <= 1e-6 * bound + 1e-6)
 
 
 @pytest.mark.parametrize("cfg", [
@@ -180,8 +205,8 @@ def test_projection_matches_oracle():
     mgr = synth_manager(s)
     lib = _alut.load()
     t = mgr.alut_tables()
-    x = s["x"].float().to(DEV)
-    b = _alut.make_batch(x, s["sel"].to(DEV), s["vis"].to(DEV), None)
+    x, selb, visb = s["x"].float().to(DEV), s["sel"].to(DEV), s["vis"].to(DEV)  # alive during the calls
+    b = _alut.make_batch(x, selb, visb, None)
     ws = torch.zeros(lib.alut_workspace_size(t, 300, 2), dtype=torch.uint8, device=DEV)
     for normalize in (False, True):
         q = torch.empty(300, 96, device=DEV)
