@@ -234,7 +234,12 @@ static bool mma_projection_ok(int key_dtype, int x_dtype, const ProjPlanArgs& a)
 
 static int launch_project(int key_dtype, int x_dtype, const ProjPlanArgs& a, cudaStream_t st) {
   const size_t smem = proj_smem_bytes(a.l);
-  if (mma_projection_ok(key_dtype, x_dtype, a)) return launch_project_kernel(k_project_mma<float>, a, smem, st);
+  if (mma_projection_ok(key_dtype, x_dtype, a)) {
+    // The cluster size may drop to 8 inside launch_project_kernel; size for the larger layout.
+    const size_t sm = std::max(mma_smem_layout(a.l, a.h, a.nsplit).total,
+                               mma_smem_layout(a.l, a.h, std::min(a.nsplit, 8)).total);
+    return launch_project_kernel(k_project_mma<float>, a, sm, st);
+  }
   switch (key_dtype) {
     case ALUT_F32: return launch_project_k<float>(x_dtype, a, smem, st);
     case ALUT_BF16: return launch_project_k<__nv_bfloat16>(x_dtype, a, smem, st);

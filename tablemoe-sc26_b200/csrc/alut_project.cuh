@@ -162,10 +162,11 @@ __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
 // Bias, rounding to the key dtype and optional L2 normalisation of rows [r0, r1) of a
 // finished tile (search.py:12-21, :484-488). One warp per row.
 template <typename TK>
-__device__ void finish_rows(const ProjPlanArgs& a, float* tile, int q0, int r0, int r1, const int* mod,
-                            const float (*bias)[kMaxL]) {
+__device__ void finish_rows(const ProjPlanArgs& a, float* tile_base, int q0, int r0, int r1, const int* mod,
+                            const float (*bias)[kMaxL], int tile_row0 = 0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L = a.l;
+  float* tile = tile_base - static_cast<int64_t>(tile_row0) * L;  // tile[r * L] for r in [r0, r1)
   for (int r = r0 + warp; r < r1; r += kProjThreads / 32) {
     const float* b = bias[mod[r]];
     float ss = 0.f;
@@ -466,7 +467,30 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-constexpr int kMmaKBlock = 8;  // k-steps (x 16 rows of H) whose fragments are loaded together
+constexpr int kMmaKBlock = 8;             // k-steps whose fragments are loaded together
+constexpr size_t kMmaStageBudget = 160 * 1024;  // shared memory for a staged basis slice
+
+// Shared memory of k_project_mma: the CTA's slice of the split basis (both modalities,
+// 3 parts, L columns, rows of krange k padded by 16 bytes so fragment loads of 8 columns
+// hit different banks) when it fits, then the receive buffer of the cluster reduction
+// ([nsplit][rows_per][L] fp32 partial rows pushed by every rank to the row's owner).
+struct MmaSmem {
+  int krange, pitch;  // elements of k per slice row, bytes per padded slice row
+  bool staged;
+  size_t recv, total;
+};
+__host__ __device__ inline MmaSmem mma_smem_layout(int l, int h, int nsplit) {
+  MmaSmem m;
+  const int ksteps = h / 16;
+  m.krange = ((ksteps + nsplit - 1) / nsplit) * 16;
+  m.pitch = m.krange * 2 + 16;
+  const size_t sb = static_cast<size_t>(6) * l * m.pitch;
+  m.staged = sb <= kMmaStageBudget;
+  m.recv = m.staged ? align256(sb) : 0;
+  const int rows_per = (kProjTileQ + nsplit - 1) / nsplit;
+  m.total = m.recv + align256(sizeof(float) * static_cast<size_t>(nsplit) * rows_per * l);
+  return m;
+}
 
 template <typename TK>
 __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
@@ -480,9 +504,8 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   const int sp = blockIdx.x % a.nsplit;
   const int q0 = qt * kProjTileQ;
   const int nq = min(kProjTileQ, a.q - q0);
-  const ProjSmem lay = proj_smem_layout(L);
-  float* tile = reinterpret_cast<float*>(psm + lay.tile);
-  float* red = reinterpret_cast<float*>(psm + lay.red);
+  const MmaSmem lay = mma_smem_layout(L, H, a.nsplit);
+  float* recv = reinterpret_cast<float*>(psm + lay.recv);
   __shared__ int mod[kProjTileQ];
   __shared__ int need[2];
   __shared__ float s_bias[2][kMaxL];
@@ -491,18 +514,20 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   const int k_end = static_cast<int>(static_cast<int64_t>(sp + 1) * ksteps / a.nsplit);
   const int ntiles = L / 8;
   const int64_t plane = static_cast<int64_t>(L) * H;
-  const uint32_t* ps32 = reinterpret_cast<const uint32_t*>(a.proj_split);
-  // Static data first: biases, and an L2 prefetch of this CTA's slice of the split basis.
+  // Static data first (overlaps the predecessor under programmatic launch): biases and the
+  // CTA's slice of the split basis, both modalities, into shared memory.
   for (int i = tid; i < 2 * L; i += kProjThreads)
     s_bias[i / L][i % L] = static_cast<const float*>(a.bias[i / L])[i % L];
-  {
-    const int rows = 2 * 3 * L;  // (modality, part, column) rows of H elements
-    const int64_t kb = static_cast<int64_t>(k_begin) * 16, kn = static_cast<int64_t>(k_end - k_begin) * 16;
-    for (int r = tid; r < rows; r += kProjThreads) {
-      const char* base = reinterpret_cast<const char*>(a.proj_split + static_cast<int64_t>(r) * H + kb);
-      for (int64_t off = 0; off < kn * 2; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
+  const int kn16 = (k_end - k_begin) * 16;  // elements of k in this slice
+  if (lay.staged) {
+    const int units = kn16 / 8;  // 16-byte units per slice row
+    for (int i = tid; i < 6 * L * units; i += kProjThreads) {
+      const int row = i / units, u = i % units;  // row = (m*3 + part)*L + col
+      cp_async16(psm + static_cast<size_t>(row) * lay.pitch + u * 16,
+                 a.proj_split + static_cast<int64_t>(row) * H + static_cast<int64_t>(k_begin) * 16 + u * 8);
     }
   }
+  cp_async_commit();
   pdl_wait();
   if (a.zero_best && blockIdx.x == 0)
     for (int i = tid; i < a.zero_n; i += kProjThreads) a.zero_best[i] = 0ull;
@@ -513,12 +538,19 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
     mod[tid] = m;
     if (tid < nq) need[m] = 1;
   }
-  __syncthreads();
-  ALUT_TRACE(1);
   const bool row0_ok = gq < nq, row1_ok = gq + 8 < nq;
-  const int m_r0 = mod[gq], m_r1 = mod[gq + 8];
   const __nv_bfloat16* xr0 = static_cast<const __nv_bfloat16*>(a.x) + static_cast<int64_t>(q0 + (row0_ok ? gq : 0)) * a.x_stride;
   const __nv_bfloat16* xr1 = static_cast<const __nv_bfloat16*>(a.x) + static_cast<int64_t>(q0 + (row1_ok ? gq + 8 : 0)) * a.x_stride;
+  cp_async_wait<0>();
+  __syncthreads();
+  ALUT_TRACE(1);
+  const int m_r0 = mod[gq], m_r1 = mod[gq + 8];
+  const int rows_per = (kProjTileQ + a.nsplit - 1) / a.nsplit;
+  cg::cluster_group cluster = cg::this_cluster();
+  // Every CTA of the cluster must be running before any writes into its shared memory:
+  // arrive now, wait just before the first remote store (the MMAs run in between).
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  bool cluster_ready = false;
   for (int nt = warp; nt < ntiles; nt += kProjThreads / 32) {
     float c[4] = {0.f, 0.f, 0.f, 0.f};
     for (int kb = k_begin; kb < k_end; kb += kMmaKBlock) {
@@ -539,58 +571,63 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
         if (!need[m]) continue;
         // Rows of the other modality are zeroed in A, so the two passes add exactly.
         const uint32_t keep0 = (m_r0 == m) ? 0xffffffffu : 0u, keep1 = (m_r1 == m) ? 0xffffffffu : 0u;
-        const uint32_t* bcol = ps32 + (static_cast<int64_t>(m) * 3 * plane + static_cast<int64_t>(nt * 8 + gq) * H) / 2;
-        uint32_t bf[kMmaKBlock][3][2];
-#pragma unroll
-        for (int s = 0; s < kMmaKBlock; ++s) {
-          if (s < kn) {
-            const int64_t k0 = static_cast<int64_t>(kb + s) * 16 + 2 * tq;
-#pragma unroll
-            for (int part = 0; part < 3; ++part) {
-              bf[s][part][0] = bcol[(part * plane + k0) / 2];
-              bf[s][part][1] = bcol[(part * plane + k0 + 8) / 2];
-            }
-          }
-        }
 #pragma unroll
         for (int s = 0; s < kMmaKBlock; ++s) {
           if (s < kn) {
             const uint32_t am[4] = {xa[s][0] & keep0, xa[s][1] & keep1, xa[s][2] & keep0, xa[s][3] & keep1};
+            const int kl = (kb + s - k_begin) * 16 + 2 * tq;  // k within the slice
 #pragma unroll
-            for (int part = 0; part < 3; ++part) mma_bf16_16816(c, am, bf[s][part][0], bf[s][part][1]);
+            for (int part = 0; part < 3; ++part) {
+              const int row = (m * 3 + part) * L + nt * 8 + gq;
+              uint32_t b0, b1;
+              if (lay.staged) {
+                const unsigned char* br = psm + static_cast<size_t>(row) * lay.pitch;
+                b0 = *reinterpret_cast<const uint32_t*>(br + kl * 2);
+                b1 = *reinterpret_cast<const uint32_t*>(br + kl * 2 + 16);
+              } else {
+                const __nv_bfloat16* bg = a.proj_split + static_cast<int64_t>(row) * H + static_cast<int64_t>(k_begin) * 16 + kl;
+                b0 = *reinterpret_cast<const uint32_t*>(bg);
+                b1 = *reinterpret_cast<const uint32_t*>(bg + 8);
+              }
+              mma_bf16_16816(c, am, b0, b1);
+            }
           }
         }
       }
     }
+    // Push the partial rows to their owners' receive buffers (slot = this rank).
+    if (!cluster_ready) {
+      asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+      cluster_ready = true;
+    }
     const int col = nt * 8 + 2 * tq;
-    tile[gq * L + col] = c[0];
-    tile[gq * L + col + 1] = c[1];
-    tile[(gq + 8) * L + col] = c[2];
-    tile[(gq + 8) * L + col + 1] = c[3];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = gq + 8 * half;
+      const int owner = r / rows_per;
+      float* dst = cluster.map_shared_rank(recv, owner) + (static_cast<size_t>(sp) * rows_per + r % rows_per) * L + col;
+      dst[0] = c[2 * half];
+      dst[1] = c[2 * half + 1];
+    }
   }
+  if (!cluster_ready) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // warps without n-tiles
   ALUT_TRACE(5);
-  if (a.nsplit == 1) {
-    __syncthreads();
-    finish_rows<TK>(a, tile, q0, 0, nq, mod, s_bias);
-    return;
-  }
-  cg::cluster_group cluster = cg::this_cluster();
-  cluster.sync();
+  cluster.sync();  // every partial row has arrived at its owner; nothing remote is read after this
   ALUT_TRACE(6);
-  const int rows_per = (kProjTileQ + a.nsplit - 1) / a.nsplit;
+  // The owner of rows [r0, r1) sums the ranks' partials in rank order and finishes them.
   const int r0 = min(nq, sp * rows_per);
   const int r1 = min(nq, r0 + rows_per);
-  for (int i = r0 * L + tid; i < r1 * L; i += kProjThreads) {
+  // In place: element (rr, c) of slot 0 is read and written by one thread only.
+  for (int i = tid; i < (r1 - r0) * L; i += kProjThreads) {
+    const int rr = i / L, c2 = i % L;
     float v = 0.f;
-    for (int k = 0; k < a.nsplit; ++k) v += cluster.map_shared_rank(tile, k)[i];
-    red[i] = v;
+    for (int k = 0; k < a.nsplit; ++k) v += recv[(static_cast<size_t>(k) * rows_per + rr) * L + c2];
+    recv[static_cast<size_t>(rr) * L + c2] = v;
   }
   __syncthreads();
   ALUT_TRACE(7);
-  finish_rows<TK>(a, red, q0, r0, r1, mod, s_bias);
+  finish_rows<TK>(a, recv, q0, r0, r1, mod, s_bias, r0);
   ALUT_TRACE(8);
-  cluster.sync();
-  ALUT_TRACE(9);
 }
 
 }  // namespace alut
