@@ -46,6 +46,9 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 KERNELS_PER_LAYER = 3  # project+plan, centroid scan, gather/combine
 CPU_LAYERS = 4
 PROFILE_STEPS = 20  # replays of the event-instrumented step graph for the scan-kernel timing
+# DRAM bytes (read + write) per layer of k_project_mma + k_search_decode, from one ncu
+# capture of this workload's layer shape (profiles/decode_kernels_full_qwen3vl_c2.md).
+NCU_TRAFFIC_PER_LAYER = 1_698_048 + 12_360_448
 
 
 def dist_env():
@@ -360,7 +363,7 @@ def run_alut(args, rank, world, local, device):
         achieved = bpl / (avg_ms / 1e3) / 1e9
         roofline = {"kernel": "k_project + k_search_decode (projection + centroid scan)", "bound": "hbm", "achieved": round(achieved, 1),
                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                    "traffic": None, "peak_source": peak_src, "bytes_per_launch": int(bpl),
+                    "traffic": NCU_TRAFFIC_PER_LAYER, "peak_source": peak_src, "bytes_per_launch": int(bpl),
                     "launch_us": round(avg_ms * 1e3, 2), "launches_timed": len(scan_ms),
                     "timed_span": "projection + centroid scan (the scan is launched as a programmatic "
                                   "dependent of the projection and streams keys while it runs)"}
