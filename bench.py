@@ -166,6 +166,16 @@ def barrier(world):
         dist.barrier()
 
 
+def sum_over_ranks(v, world, device):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.int64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return int(t.item())
+
+
 def max_over_ranks(v, world, device):
     if world == 1:
         return v
@@ -329,7 +339,7 @@ def run_alut(args, rank, world, local, device):
         barrier(world)
     dev_ms = max_over_ranks(start.elapsed_time(stop), world, device)
     ms_per_step = dev_ms / args.steps
-    total_lookups = lookups_per_step * args.steps * world
+    total_lookups = sum_over_ranks(lookups_per_step, world, device) * args.steps
     value = total_lookups / (dev_ms / 1e3)
     scan_ms = []
     for _ in range(PROFILE_STEPS):
@@ -382,7 +392,7 @@ def run_alut(args, rank, world, local, device):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random tables and routing)", "config": config_dict(world),
-            "lookups_per_step": lookups_per_step * world,
+            "lookups_per_step": total_lookups // args.steps,
             "e2e": {"value": round(total_lookups / (e2e_ms / 1e3), 1), "unit": "lookups/s",
                     "h2d_bytes_per_step": e2e.h2d_bytes, "d2h_bytes_per_step": e2e.d2h_bytes,
                     "ms_per_step": round(e2e_ms / args.steps, 5)},

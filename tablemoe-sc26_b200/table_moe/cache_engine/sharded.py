@@ -1,0 +1,145 @@
+"""One very large centroid table split by centroid range over the ranks of a process group.
+
+Rank r of W holds centroids [K*r/W, K*(r+1)/W) of the key table and the matching value
+rows. A lookup of Q tokens then runs in three steps:
+
+1. every rank scans its slice for all Q tokens (``alut_search_packed``), producing one
+   packed candidate per token: ``(order-preserving score bits << 32) | (0xFFFFFFFF - global
+   index)``, so that the largest packed value is the best score with the lowest index;
+2. the W candidate vectors are exchanged (``all_gather_into_tensor``, 8 bytes per token per
+   rank) and merged by max (``alut_merge_packed``), which also applies the hit rule - every
+   rank now holds the winners;
+3. each rank gathers the winning rows it owns (rows owned elsewhere, and misses, come out
+   as zeros) and a ``reduce_scatter_tensor`` (sum) hands each rank its slice of Q/W tokens;
+   a row has one non-zero contribution, so the sum is an exact copy.
+
+The reference is single-GPU; this is the centroid-range sharding the benchmark's large-
+table configuration asks for. The device work goes through the C ABI; the three device
+steps are attributes of the object so that the exchange logic can be exercised on CPU
+process groups (gloo) with stand-ins.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _alut
+
+
+def shard_range(k_total: int, world: int, rank: int):
+    """Centroid rows [start, stop) held by `rank`."""
+    return k_total * rank // world, k_total * (rank + 1) // world
+
+
+class ShardedCentroidTable:
+    def __init__(self, keys, values, pca, k_total, *, group=None, keyset=_alut.KEYS_RAW,
+                 normalize=False, cmp_ge=False, thr_vision=0.0, thr_text=0.0, eps=1e-6):
+        """keys: [1, 2, Kr, L] this rank's slice (rows shard_range(k_total, W, r));
+        values: [1, 2, Kr, H]; pca: {"vision": {proj, bias}, "text": {...}}."""
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.k_total = int(k_total)
+        self.k0, self.k1 = shard_range(self.k_total, self.world, self.rank)
+        if keys.shape[2] != self.k1 - self.k0:
+            raise ValueError(f"rank {self.rank} holds {keys.shape[2]} rows, expected {self.k1 - self.k0}")
+        self.keys, self.values, self.pca = keys, values, pca
+        self.device = keys.device
+        self.params = dict(keyset=keyset, normalize=normalize, cmp_ge=cmp_ge, thr_vision=thr_vision,
+                           thr_text=thr_text, eps=eps)
+        self._tables = None
+        self._ws = None
+        # Device steps (replaceable for CPU tests of the exchange).
+        self.local_search = self._local_search
+        self.merge = self._merge
+        self.gather_owned = self._gather_owned
+
+    # ---- device steps -----------------------------------------------------------------------
+    def _tables_struct(self):
+        if self._tables is None:
+            pv, pt = self.pca["vision"], self.pca["text"]
+            k = self.keys if self.params["keyset"] == _alut.KEYS_NORMALISED else None
+            r = self.keys if self.params["keyset"] == _alut.KEYS_RAW else None
+            self._tables = _alut.make_tables(k, r, self.values, pv["proj"], pv["bias"], pt["proj"], pt["bias"])
+            self._split = _alut.prepare_basis(self._tables, self.device)
+            if self._split is not None:
+                self._tables.proj_split = self._split.data_ptr()
+        return self._tables
+
+    def _params_struct(self):
+        p = self.params
+        return _alut.make_params(p["keyset"], p["normalize"], p["cmp_ge"], p["thr_vision"], p["thr_text"], p["eps"])
+
+    def _local_search(self, x, is_vision):
+        """Packed best candidate of every token over this rank's slice -> int64 [Q]."""
+        lib = _alut.load()
+        q = x.shape[0]
+        t = self._tables_struct()
+        need = int(lib.alut_workspace_size(t, q, 1))
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        sel = torch.zeros(q, 1, dtype=torch.int64, device=self.device)
+        vis = is_vision.reshape(-1).bool().contiguous()
+        packed = torch.empty(q, dtype=torch.int64, device=self.device)
+        b = _alut.make_batch(x, sel, vis, None)  # x, sel, vis stay referenced until the call returns
+        rc = lib.alut_search_packed(t, ctypes.byref(b), self._params_struct(), None, self.k0, packed.data_ptr(),
+                                    self._ws.data_ptr(), self._ws.numel(), _alut.stream_ptr(self.device))
+        _alut.check(rc, "alut_search_packed")
+        return packed
+
+    def _merge(self, packed_all, is_vision):
+        """[W, Q] packed candidates -> (hit [Q] bool, idx [Q] int64 global)."""
+        lib = _alut.load()
+        w, q = packed_all.shape
+        vis = is_vision.reshape(-1).bool().contiguous()
+        hit = torch.empty(q, dtype=torch.bool, device=self.device)
+        idx = torch.empty(q, dtype=torch.int64, device=self.device)
+        rc = lib.alut_merge_packed(w, q, 1, packed_all.data_ptr(), vis.data_ptr(), self._params_struct(),
+                                   hit.data_ptr(), idx.data_ptr(), _alut.stream_ptr(self.device))
+        _alut.check(rc, "alut_merge_packed")
+        return hit, idx
+
+    def _gather_owned(self, hit, idx, is_vision):
+        """[Q, H] rows of the winners this rank owns; other rows are zero."""
+        lib = _alut.load()
+        q = idx.shape[0]
+        owned = hit & (idx >= self.k0) & (idx < self.k1)
+        cids = torch.where(owned, idx - self.k0, torch.full_like(idx, -1)).contiguous()
+        eids = torch.zeros(q, dtype=torch.int64, device=self.device)
+        mids = torch.where(is_vision.reshape(-1).bool(), 0, 1).to(torch.int64).contiguous()
+        out = torch.empty(q, self.values.shape[-1], dtype=self.values.dtype, device=self.device)
+        rc = lib.alut_gather_rows(self._tables_struct(), q, eids.data_ptr(), mids.data_ptr(), cids.data_ptr(), None,
+                                  out.data_ptr(), out.stride(0), _alut.stream_ptr(self.device))
+        _alut.check(rc, "alut_gather_rows")
+        return out
+
+    # ---- lookup ---------------------------------------------------------------------------
+    def search(self, x, is_vision):
+        """Global (hit, idx) of every token, identical on all ranks."""
+        packed = self.local_search(x, is_vision)
+        if self.world == 1:
+            return self.merge(packed.view(1, -1), is_vision)
+        flat = torch.empty(self.world * packed.numel(), dtype=packed.dtype, device=packed.device)
+        dist.all_gather_into_tensor(flat, packed.contiguous(), group=self.group)
+        return self.merge(flat.view(self.world, -1), is_vision)
+
+    def lookup(self, x, is_vision):
+        """Search, then the value rows of this rank's token slice [Q*r/W, Q*(r+1)/W) (Q must
+        be a multiple of W): (hit [Q], idx [Q], rows [Q/W, H])."""
+        hit, idx = self.search(x, is_vision)
+        rows = self.gather_owned(hit, idx, is_vision)
+        if self.world == 1:
+            return hit, idx, rows
+        q = rows.shape[0]
+        if q % self.world:
+            raise ValueError(f"token count {q} is not a multiple of the world size {self.world}")
+        n = q // self.world
+        if dist.get_backend(self.group) == "gloo":  # CPU groups: no reduce_scatter in gloo
+            rows = rows.contiguous().clone()
+            dist.all_reduce(rows, op=dist.ReduceOp.SUM, group=self.group)
+            return hit, idx, rows[self.rank * n:(self.rank + 1) * n]
+        mine = torch.empty(n, rows.shape[1], dtype=rows.dtype, device=rows.device)
+        dist.reduce_scatter_tensor(mine, rows.contiguous(), op=dist.ReduceOp.SUM, group=self.group)
+        return hit, idx, mine
