@@ -101,6 +101,10 @@ typedef struct alut_tables {
    * (hi + mid + lo == proj to fp32 precision), written by alut_prepare_basis. When set and
    * x is bf16, small batches project on tensor cores; NULL keeps the CUDA-core path. */
   const void* proj_split;
+  /* Optional: fp32 key tables prepared for the tensor-core scan by alut_prepare_keys
+   * (keys_split for keys, raw_keys_split for raw_keys; NULL keeps the CUDA-core scans). */
+  const void* keys_split;
+  const void* raw_keys_split;
 } alut_tables_t;
 
 /* One batch of routed tokens. */
@@ -141,6 +145,17 @@ size_t alut_basis_split_bytes(const alut_tables_t* tables);
 /* Write the split basis (see alut_tables_t.proj_split) of tables->proj into out, a device
  * buffer of alut_basis_split_bytes() bytes. Once per table load; the basis is static. */
 int alut_prepare_basis(const alut_tables_t* tables, void* out, size_t out_bytes, alut_stream_t stream);
+
+/* Bytes of the tensor-core form of one fp32 key set of these tables (0 if they do not
+ * qualify: fp32 keys, L % 16 == 0, L <= 128): every (expert, modality) table cut into
+ * 128-row chunks, each chunk as two bf16 parts (hi, lo = keys - hi) in the tensor cores'
+ * K-major core-matrix order, followed by the largest row norm of every table. */
+size_t alut_keys_split_bytes(const alut_tables_t* tables);
+
+/* Write that form of the key set `keyset` into out (device, alut_keys_split_bytes bytes).
+ * Once per table load; the keys are static. */
+int alut_prepare_keys(const alut_tables_t* tables, int32_t keyset, void* out, size_t out_bytes,
+                      alut_stream_t stream);
 
 /* a1: q_low[Q,L] = x[mask_m] @ proj_m + bias_m per modality, optionally L2-normalised,
  * written in the key dtype (search.py:476-498). */

@@ -11,6 +11,7 @@
 #include "alut_common.cuh"
 #include "alut_project.cuh"
 #include "alut_search.cuh"
+#include "alut_tc.cuh"
 
 namespace alut {
 
@@ -419,6 +420,52 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     }
     return ALUT_OK;
   }
+  // Large batches on fp32 tables prepared for it: tensor-core scan (tcgen05).
+  const void* ksplit = keys == t->raw_keys ? t->raw_keys_split : t->keys_split;
+  if (ksplit && t->key_dtype == ALUT_F32 && t->l % 16 == 0 && t->l <= kTcMaxL && pairs >= kTcMinPairs &&
+      t->key_stride[2] >= t->l) {
+    a.group = kTcRows;
+    int rc = launch_plan(a, st);
+    if (rc) return rc;
+    rc = launch_project(t->key_dtype, b->x_dtype, a, st);
+    if (rc) return rc;
+    TcArgs c{};
+    const int ntab = 2 * t->num_experts;
+    const int nchunks = ceil_div(t->k, kTcRows);
+    c.ksplit = static_cast<const unsigned char*>(ksplit);
+    c.knorm = reinterpret_cast<const float*>(static_cast<const char*>(ksplit) +
+                                             align256(static_cast<size_t>(ntab) * nchunks * tc_chunk_bytes(t->l)));
+    c.keys = static_cast<const float*>(keys);
+    c.key_stride_e = t->key_stride[0];
+    c.key_stride_m = t->key_stride[1];
+    c.key_stride_k = t->key_stride[2];
+    c.k = t->k;
+    c.l = t->l;
+    c.s = b->s;
+    c.nchunks = nchunks;
+    c.idx_offset = idx_offset;
+    c.qlow = a.qlow;
+    c.sorted = a.sorted;
+    c.groups = a.groups;
+    c.meta = a.meta;
+    c.best = best;
+    c.err = a.meta + 1;
+    const size_t smem = search_tc_smem_bytes(t->l);
+    rc = allow_smem(reinterpret_cast<const void*>(k_search_tc), smem);
+    if (rc) return rc;
+    if (g_prof_start && g_prof_stop) {
+      cudaError_t e = cudaEventRecordWithFlags(g_prof_start, st, cudaEventRecordExternal);
+      if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
+    }
+    k_search_tc<<<num_sms(), kTcThreads, smem, st>>>(c);
+    rc = check_launch("k_search_tc");
+    if (rc) return rc;
+    if (g_prof_start && g_prof_stop) {
+      cudaError_t e = cudaEventRecordWithFlags(g_prof_stop, st, cudaEventRecordExternal);
+      if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
+    }
+    return ALUT_OK;
+  }
   int rc = launch_plan(a, st);
   if (rc) return rc;
   rc = launch_project(t->key_dtype, b->x_dtype, a, st);
@@ -499,6 +546,30 @@ int alut_set_profile_events(void* start_event, void* stop_event) {
 }
 
 const char* alut_last_error(void) { return g_err; }
+
+size_t alut_keys_split_bytes(const alut_tables_t* t) {
+  if (!t || t->key_dtype != ALUT_F32 || t->l <= 0 || t->l % 16 != 0 || t->l > kTcMaxL || t->k <= 0 ||
+      t->num_experts <= 0)
+    return 0;
+  const int64_t ntab = 2 * static_cast<int64_t>(t->num_experts);
+  const int64_t nchunks = (t->k + kTcRows - 1) / kTcRows;
+  return align256(ntab * nchunks * tc_chunk_bytes(t->l)) + align256(sizeof(float) * ntab);
+}
+
+int alut_prepare_keys(const alut_tables_t* t, int32_t keyset, void* out, size_t out_bytes, alut_stream_t stream) {
+  const size_t need = alut_keys_split_bytes(t);
+  if (need == 0) return fail(ALUT_EINVAL, "prepare_keys: tables do not qualify (fp32 keys, l%%16, l<=%d)", kTcMaxL);
+  if (!out || out_bytes < need) return fail(ALUT_EINVAL, "prepare_keys: out needs %zu bytes", need);
+  const void* keys = keyset == ALUT_KEYS_RAW ? t->raw_keys : (keyset == ALUT_KEYS_NORMALISED ? t->keys : nullptr);
+  if (!keys) return fail(ALUT_EINVAL, "prepare_keys: key set %d is NULL", keyset);
+  const int ntab = 2 * t->num_experts;
+  const int nchunks = (t->k + kTcRows - 1) / kTcRows;
+  const size_t body = align256(static_cast<size_t>(ntab) * nchunks * tc_chunk_bytes(t->l));
+  k_prepare_keys<<<1184, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const float*>(keys), t->key_stride[0], t->key_stride[1], t->key_stride[2], ntab, t->k, t->l,
+      nchunks, static_cast<__nv_bfloat16*>(out), reinterpret_cast<float*>(static_cast<char*>(out) + body));
+  return check_launch("k_prepare_keys");
+}
 
 size_t alut_basis_split_bytes(const alut_tables_t* t) {
   if (!t || t->proj_dtype != ALUT_F32 || t->h <= 0 || t->l <= 0 || t->h % 16 != 0 || t->l % 8 != 0) return 0;

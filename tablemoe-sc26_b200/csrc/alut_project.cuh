@@ -49,6 +49,9 @@ struct ProjPlanArgs {
   int* meta;
   // tensor-core projection: bf16 split basis [2][3][L][H] (see alut_prepare_basis)
   const __nv_bfloat16* proj_split;
+  // plan: slots per search group (kSearchGroup for the CUDA-core scans, 128 for the
+  // tensor-core scan); 0 means kSearchGroup
+  int group;
 };
 
 // Tokens per thread (a thread owns one column l of NOUT tokens; 16/NOUT token groups of L
@@ -101,6 +104,7 @@ __device__ __forceinline__ int block_exclusive_scan_256(int v, int* scratch, int
 __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
   extern __shared__ __align__(16) int plan_smem[];
   const int tid = threadIdx.x;
+  const int G = a.group > 0 ? a.group : kSearchGroup;
   const int ntab = 2 * a.num_experts;
   const int64_t pairs = static_cast<int64_t>(a.q) * a.s;
   int* counts = plan_smem;
@@ -130,17 +134,17 @@ __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
   int lc = 0, lg = 0;
   for (int t = t0; t < t1; ++t) {
     lc += counts[t];
-    lg += (counts[t] + kSearchGroup - 1) / kSearchGroup;
+    lg += (counts[t] + G - 1) / G;
   }
   int bc = block_exclusive_scan_256(lc, scan_scratch, &s_tot_c);
   int bg = block_exclusive_scan_256(lg, scan_scratch, &s_tot_g);
   for (int t = t0; t < t1; ++t) {
     offs[t] = bc;
     const int c = counts[t];
-    for (int g = 0; g * kSearchGroup < c; ++g)
-      a.groups[bg + g] = make_int4(t, bc + g * kSearchGroup, min(kSearchGroup, c - g * kSearchGroup), 0);
+    for (int g = 0; g * G < c; ++g)
+      a.groups[bg + g] = make_int4(t, bc + g * G, min(G, c - g * G), 0);
     bc += c;
-    bg += (c + kSearchGroup - 1) / kSearchGroup;
+    bg += (c + G - 1) / G;
   }
   if (tid == 0) a.meta[0] = s_tot_g;
   __syncthreads();

@@ -56,10 +56,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Wait with an iteration limit; false if the limit was reached.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait with a deadline of kWaitNs (each try_wait may itself suspend for a while, so the
+// bound is on time, not on the number of tries); false if the deadline passed.
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (uint32_t n = 0; n < kWaitLimit; ++n)
+  const uint64_t t0 = global_ns();
+  for (uint32_t n = 0; n < kWaitLimit; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > kWaitNs) return false;
+  }
   return false;
 }
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

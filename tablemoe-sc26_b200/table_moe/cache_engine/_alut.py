@@ -36,6 +36,7 @@ class Tables(ctypes.Structure):
         ("proj", ctypes.c_void_p * 2), ("bias", ctypes.c_void_p * 2),
         ("key_stride", ctypes.c_int64 * 3), ("value_stride", ctypes.c_int64 * 3),
         ("proj_stride_h", ctypes.c_int64), ("proj_split", ctypes.c_void_p),
+        ("keys_split", ctypes.c_void_p), ("raw_keys_split", ctypes.c_void_p),
     ]
 
 
@@ -67,6 +68,8 @@ _PP = ctypes.POINTER(SearchParams)
 SIGNATURES = {
     "alut_workspace_size": (_SZ, [_TP, _I32, _I32]),
     "alut_basis_split_bytes": (_SZ, [_TP]),
+    "alut_keys_split_bytes": (_SZ, [_TP]),
+    "alut_prepare_keys": (ctypes.c_int, [_TP, _I32, _P, _SZ, _P]),
     "alut_prepare_basis": (ctypes.c_int, [_TP, _P, _SZ, _P]),
     "alut_project": (ctypes.c_int, [_TP, _BP, _I32, ctypes.c_float, _P, _I64, _P, _SZ, _P]),
     "alut_search": (ctypes.c_int, [_TP, _BP, _PP, _P, _P, _P, _I64, _P, _SZ, _P]),

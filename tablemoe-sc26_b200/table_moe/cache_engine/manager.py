@@ -119,8 +119,30 @@ class HybridStorageManager:
             self._proj_split = _alut.prepare_basis(t, self.device) if self.device.type == "cuda" else None
             if self._proj_split is not None:
                 t.proj_split = self._proj_split.data_ptr()
+            self._keys_split = {}
             self._tables = (key, t)
         return self._tables[1]
+
+    def prepare_tensor_core(self, keyset):
+        """The tensor-core form of one key set (``_alut.KEYS_RAW`` or ``KEYS_NORMALISED``):
+        made once, on the first batch large enough to use it (it takes as much memory as
+        that key set). Tables that do not qualify (not fp32, L % 16, L > 128) are left alone."""
+        t = self.alut_tables()
+        if keyset in self._keys_split or self.device.type != "cuda":
+            return t
+        lib = _alut.load()
+        n = int(lib.alut_keys_split_bytes(t))
+        buf = None
+        if n:
+            buf = torch.empty(n, dtype=torch.uint8, device=self.device)
+            _alut.check(lib.alut_prepare_keys(t, int(keyset), buf.data_ptr(), n, _alut.stream_ptr(self.device)),
+                        "alut_prepare_keys")
+            if keyset == _alut.KEYS_RAW:
+                t.raw_keys_split = buf.data_ptr()
+            else:
+                t.keys_split = buf.data_ptr()
+        self._keys_split[keyset] = buf
+        return t
 
     # ---- online ring buffer (manager.py:89-155) -----------------------------------------
     @torch.no_grad()

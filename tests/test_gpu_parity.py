@@ -364,3 +364,53 @@ def test_centroid_shards_merge_to_the_full_search():
                                _alut.stream_ptr(DEV))
     _alut.check(rc, "alut_merge_packed")
     assert torch.equal(hit, full_hit[:, 0]) and torch.equal(idx, full_idx[:, 0])
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(name="c3_tc", Q=4096, S=8, E=128, K=1024, L=64, H=2048, reuse_p=0.4, vis_frac=0.25, zipf=1.1),
+    dict(name="c5_like", Q=1024, S=1, E=1, K=8192, L=128, H=512, reuse_p=1.1),
+    dict(name="ragged_k", Q=600, S=2, E=3, K=300, L=48, H=256, reuse_p=0.9),
+])
+def test_tensor_core_scan_matches_oracle(cfg):
+    """Large batches on fp32 tables take the tcgen05 scan (bf16 split candidates + exact fp32
+    rescoring); the indices must still follow the exact fp32 argmax."""
+    cfg = dict(cfg)
+    name = cfg.pop("name")
+    s = synth(**cfg)
+    mgr = synth_manager(s)
+    hit, idx = gpu_dot(mgr, s)
+    assert mgr._keys_split.get(_alut.KEYS_RAW) is not None, "tensor-core key form was not prepared"
+    q, keys, rh, ri = oracle_dot(s)
+    check_search(hit.cpu().numpy(), idx.cpu().numpy(), rh, ri, q, keys, s["sel"].numpy(), s["vis"].numpy(),
+                 (0.0, 0.0), "float32", what=name)
+
+
+def test_tensor_core_scan_ties_and_negative_scores():
+    """Duplicate keys in different 128-row chunks tie to the lowest index; rows whose every
+    score is negative still return their (negative) maximum under a >= -inf rule."""
+    Q, K, L = 640, 1024, 64
+    s = synth(Q=Q, S=1, E=1, K=K, L=L, H=128, seed=12, reuse_p=1.1)
+    q = orc.project(s["x"].float().numpy(), s["vis"].numpy(), s["proj"].numpy(), s["bias"].numpy())
+    raw = -torch.rand(1, 2, K, L) * 0.01 - 0.001
+    for t in range(8):
+        m = 0 if bool(s["vis"][t]) else 1
+        for k in (900 - t, 300 + t, 131 + t):
+            raw[0, m, k] = torch.from_numpy(q[t]) * 3
+    s["raw"] = raw
+    mgr = synth_manager(s)
+    eng = VectorSearchEngine(mgr)
+    x, sel, vis, reuse = s["x"].float().to(DEV), s["sel"].to(DEV), s["vis"].to(DEV), s["reuse"].to(DEV)
+    old = CacheConfig.OFFLINE_DOT_THRESHOLD
+    CacheConfig.OFFLINE_DOT_THRESHOLD = -1e30
+    try:
+        hit, idx = eng.search_prefill_offline_dot(0, x, sel, vis, reuse)
+    finally:
+        CacheConfig.OFFLINE_DOT_THRESHOLD = old
+    assert mgr._keys_split.get(_alut.KEYS_RAW) is not None
+    assert idx[:8, 0].cpu().tolist() == [131 + t for t in range(8)]
+    keys = raw.float().numpy()
+    rh, ri, _, _ = orc.search(q, keys, s["sel"].numpy(), s["vis"].numpy(), s["reuse"].numpy(), -1e30, -1e30,
+                              cmp_ge=False)
+    assert hit.all()
+    check_search(hit.cpu().numpy(), idx.cpu().numpy(), rh, ri, q, keys, s["sel"].numpy(), s["vis"].numpy(),
+                 (-1e30, -1e30), "float32", what="tc ties")
