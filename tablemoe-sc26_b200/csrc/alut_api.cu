@@ -27,6 +27,19 @@ static int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+// Records a profiling event (alut_set_profile_events) around the scan: as an external event
+// node while the stream is being captured into a graph, as a plain record otherwise.
+static int record_profile(cudaEvent_t ev, cudaStream_t st) {
+  if (!ev) return ALUT_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(st, &cs);
+  if (e == cudaSuccess)
+    e = cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal)
+                                            : cudaEventRecord(ev, st);
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
+  return ALUT_OK;
+}
+
 static int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(ALUT_ECUDA, "%s: %s", what, cudaGetErrorString(e));
@@ -386,10 +399,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     // dependent, whose key copies overlap the projection.
     a.zero_best = best;
     a.zero_n = pairs;
-    if (g_prof_start && g_prof_stop) {
-      cudaError_t e = cudaEventRecordWithFlags(g_prof_start, st, cudaEventRecordExternal);
-      if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
-    }
+    if (g_prof_start && g_prof_stop && record_profile(g_prof_start, st)) return ALUT_ECUDA;
     int rc = launch_project(t->key_dtype, b->x_dtype, a, st);
     if (rc) return rc;
     DecodeScanArgs d{};
@@ -414,10 +424,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     d.err = a.meta + 1;
     rc = launch_search_decode(t->key_dtype, d, dim3(pairs, d.s.nchunks), search_decode_smem_bytes(t->l, esz), st);
     if (rc) return rc;
-    if (g_prof_start && g_prof_stop) {
-      cudaError_t e = cudaEventRecordWithFlags(g_prof_stop, st, cudaEventRecordExternal);
-      if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
-    }
+    if (g_prof_start && g_prof_stop && record_profile(g_prof_stop, st)) return ALUT_ECUDA;
     return ALUT_OK;
   }
   // Large batches on fp32 tables prepared for it: tensor-core scan (tcgen05).
@@ -453,17 +460,11 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     const size_t smem = search_tc_smem_bytes(t->l);
     rc = allow_smem(reinterpret_cast<const void*>(k_search_tc), smem);
     if (rc) return rc;
-    if (g_prof_start && g_prof_stop) {
-      cudaError_t e = cudaEventRecordWithFlags(g_prof_start, st, cudaEventRecordExternal);
-      if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
-    }
+    if (g_prof_start && g_prof_stop && record_profile(g_prof_start, st)) return ALUT_ECUDA;
     k_search_tc<<<num_sms(), kTcThreads, smem, st>>>(c);
     rc = check_launch("k_search_tc");
     if (rc) return rc;
-    if (g_prof_start && g_prof_stop) {
-      cudaError_t e = cudaEventRecordWithFlags(g_prof_stop, st, cudaEventRecordExternal);
-      if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
-    }
+    if (g_prof_start && g_prof_stop && record_profile(g_prof_stop, st)) return ALUT_ECUDA;
     return ALUT_OK;
   }
   int rc = launch_plan(a, st);
@@ -488,10 +489,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
   s.best = best;
   const int64_t max_tiles = w.max_groups * s.nchunks;
   const int grid = static_cast<int>(std::min<int64_t>(max_tiles, static_cast<int64_t>(num_sms()) * 8));
-  if (g_prof_start && g_prof_stop) {
-    cudaError_t e = cudaEventRecordWithFlags(g_prof_start, st, cudaEventRecordExternal);
-    if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
-  }
+  if (g_prof_start && g_prof_stop && record_profile(g_prof_start, st)) return ALUT_ECUDA;
   if (tma) {
     rc = launch_search_tma(t->key_dtype, s, std::max(grid, 1), search_tma_smem_bytes(t->l, esz),
                            reinterpret_cast<int*>(a.meta) + 1, st);
@@ -499,10 +497,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     rc = launch_search(t->key_dtype, vec, s, std::max(grid, 1), search_smem_bytes(t->l), st);
   }
   if (rc) return rc;
-  if (g_prof_start && g_prof_stop) {
-    cudaError_t e = cudaEventRecordWithFlags(g_prof_stop, st, cudaEventRecordExternal);
-    if (e != cudaSuccess) return fail(ALUT_ECUDA, "profile event: %s", cudaGetErrorString(e));
-  }
+  if (g_prof_start && g_prof_stop && record_profile(g_prof_stop, st)) return ALUT_ECUDA;
   return ALUT_OK;
 }
 
