@@ -87,6 +87,11 @@ static int allow_smem(const void* kernel, size_t bytes) {
   return ALUT_OK;
 }
 
+// Tables whose keys the tensor-core scan can take (once their bf16 form is prepared).
+static bool tc_tables_ok(const alut_tables_t* t) {
+  return t && t->key_dtype == ALUT_F32 && t->l > 0 && t->l % 16 == 0 && t->l <= kTcMaxL;
+}
+
 static int check_tables(const alut_tables_t* t, bool need_proj) {
   if (!t) return fail(ALUT_EINVAL, "tables is NULL");
   if (t->num_experts <= 0 || t->k <= 0 || t->l <= 0 || t->h <= 0)
@@ -427,21 +432,22 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     if (g_prof_start && g_prof_stop && record_profile(g_prof_stop, st)) return ALUT_ECUDA;
     return ALUT_OK;
   }
-  // Large batches on fp32 tables prepared for it: tensor-core scan (tcgen05).
+  // Large batches on fp32 tables prepared for it, with room in the workspace for the staged
+  // queries: tensor-core scan (tcgen05).
   const void* ksplit = keys == t->raw_keys ? t->raw_keys_split : t->keys_split;
-  if (ksplit && t->key_dtype == ALUT_F32 && t->l % 16 == 0 && t->l <= kTcMaxL && pairs >= kTcMinPairs &&
-      t->key_stride[2] >= t->l) {
+  const Workspace wt = workspace_layout(b->q, b->s, t->l, 2 * t->num_experts, true);
+  if (ksplit && tc_tables_ok(t) && vec && pairs >= kTcMinPairs && ws_bytes >= wt.total) {
     a.group = kTcRows;
     int rc = launch_plan(a, st);
     if (rc) return rc;
     rc = launch_project(t->key_dtype, b->x_dtype, a, st);
     if (rc) return rc;
-    TcArgs c{};
     const int ntab = 2 * t->num_experts;
     const int nchunks = ceil_div(t->k, kTcRows);
+    TcArgs c{};
     c.ksplit = static_cast<const unsigned char*>(ksplit);
     c.knorm = reinterpret_cast<const float*>(static_cast<const char*>(ksplit) +
-                                             align256(static_cast<size_t>(ntab) * nchunks * tc_chunk_bytes(t->l)));
+                                             align256(static_cast<size_t>(ntab) * nchunks * tc_tile_bytes(t->l)));
     c.keys = static_cast<const float*>(keys);
     c.key_stride_e = t->key_stride[0];
     c.key_stride_m = t->key_stride[1];
@@ -450,13 +456,25 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     c.l = t->l;
     c.s = b->s;
     c.nchunks = nchunks;
+    c.stages = tc_stages(t->l);
     c.idx_offset = idx_offset;
     c.qlow = a.qlow;
+    c.qsplit = reinterpret_cast<const unsigned char*>(base + wt.qsplit);
+    c.qnorm = reinterpret_cast<const float*>(base + wt.qnorm);
     c.sorted = a.sorted;
     c.groups = a.groups;
     c.meta = a.meta;
     c.best = best;
     c.err = a.meta + 1;
+    {
+      const int64_t units = wt.tc_groups * kTcRows * (t->l / 8);
+      const int grid = static_cast<int>(std::min<int64_t>((units + 255) / 256, static_cast<int64_t>(num_sms()) * 8));
+      k_stage_queries<<<std::max(grid, 1), 256, 0, st>>>(a.qlow, t->l, b->s, a.sorted, a.groups, a.meta, wt.tc_groups,
+                                                       reinterpret_cast<__nv_bfloat16*>(base + wt.qsplit),
+                                                       reinterpret_cast<float*>(base + wt.qnorm));
+      rc = check_launch("k_stage_queries");
+      if (rc) return rc;
+    }
     const size_t smem = search_tc_smem_bytes(t->l);
     rc = allow_smem(reinterpret_cast<const void*>(k_search_tc), smem);
     if (rc) return rc;
@@ -548,7 +566,7 @@ size_t alut_keys_split_bytes(const alut_tables_t* t) {
     return 0;
   const int64_t ntab = 2 * static_cast<int64_t>(t->num_experts);
   const int64_t nchunks = (t->k + kTcRows - 1) / kTcRows;
-  return align256(ntab * nchunks * tc_chunk_bytes(t->l)) + align256(sizeof(float) * ntab);
+  return align256(ntab * nchunks * tc_tile_bytes(t->l)) + align256(sizeof(float) * ntab);
 }
 
 int alut_prepare_keys(const alut_tables_t* t, int32_t keyset, void* out, size_t out_bytes, alut_stream_t stream) {
@@ -559,10 +577,13 @@ int alut_prepare_keys(const alut_tables_t* t, int32_t keyset, void* out, size_t 
   if (!keys) return fail(ALUT_EINVAL, "prepare_keys: key set %d is NULL", keyset);
   const int ntab = 2 * t->num_experts;
   const int nchunks = (t->k + kTcRows - 1) / kTcRows;
-  const size_t body = align256(static_cast<size_t>(ntab) * nchunks * tc_chunk_bytes(t->l));
+  const size_t body = align256(static_cast<size_t>(ntab) * nchunks * tc_tile_bytes(t->l));
+  float* norms = reinterpret_cast<float*>(static_cast<char*>(out) + body);
+  cudaError_t e = cudaMemsetAsync(norms, 0, sizeof(float) * ntab, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "prepare_keys: %s", cudaGetErrorString(e));
   k_prepare_keys<<<1184, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const float*>(keys), t->key_stride[0], t->key_stride[1], t->key_stride[2], ntab, t->k, t->l,
-      nchunks, static_cast<__nv_bfloat16*>(out), reinterpret_cast<float*>(static_cast<char*>(out) + body));
+      nchunks, static_cast<__nv_bfloat16*>(out), norms);
   return check_launch("k_prepare_keys");
 }
 
@@ -584,7 +605,8 @@ int alut_prepare_basis(const alut_tables_t* t, void* out, size_t out_bytes, alut
 
 size_t alut_workspace_size(const alut_tables_t* tables, int32_t q, int32_t s) {
   if (!tables || q < 0 || s < 0 || tables->l <= 0 || tables->num_experts <= 0) return 0;
-  return workspace_layout(q, s, tables->l, 2 * tables->num_experts).total;
+  const bool tc = tc_tables_ok(tables) && static_cast<int64_t>(q) * s >= kTcMinPairs;
+  return workspace_layout(q, s, tables->l, 2 * tables->num_experts, tc).total;
 }
 
 int alut_project(const alut_tables_t* tables, const alut_batch_t* batch, int32_t normalize_q,

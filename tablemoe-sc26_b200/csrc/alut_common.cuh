@@ -203,8 +203,13 @@ struct Workspace {
   size_t best;      // uint64 [Q * S]        packed best candidate per slot
   size_t sorted;    // int32  [Q * S]        slot ids sorted by table
   size_t groups;    // int4   [max_groups]   (table, first sorted slot, count, 0)
+  // Tensor-core scan only (workspace_layout(..., tc = true)): the searched slots' queries
+  // staged per group of <= 128 slots as bf16 operand tiles, and their norms.
+  size_t qsplit;    // bf16   [tc_groups][128 * L]
+  size_t qnorm;     // f32    [tc_groups][128]
   size_t total;
   int64_t max_groups;
+  int64_t tc_groups;
 };
 
 __host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -226,7 +231,7 @@ inline int proj_splits(int q, int h) {
   return s;
 }
 
-inline Workspace workspace_layout(int q, int s, int l, int num_tables) {
+inline Workspace workspace_layout(int q, int s, int l, int num_tables, bool tc = false) {
   Workspace w{};
   const int64_t pairs = static_cast<int64_t>(q) * s;
   w.max_groups = (pairs + kSearchGroup - 1) / kSearchGroup + (pairs < num_tables ? pairs : num_tables) + 1;
@@ -236,6 +241,13 @@ inline Workspace workspace_layout(int q, int s, int l, int num_tables) {
   w.best = off;     off = align256(off + sizeof(uint64_t) * (pairs + 1));
   w.sorted = off;   off = align256(off + sizeof(int32_t) * (pairs + 1));
   w.groups = off;   off = align256(off + sizeof(int4) * w.max_groups);
+  if (tc) {
+    // Groups of <= 128 slots of one table (this bound is below max_groups, which the plan's
+    // group list uses in both cases).
+    w.tc_groups = (pairs + 127) / 128 + (pairs < num_tables ? pairs : num_tables) + 1;
+    w.qsplit = off; off = align256(off + static_cast<size_t>(w.tc_groups) * 128 * l * 2);
+    w.qnorm = off;  off = align256(off + sizeof(float) * w.tc_groups * 128);
+  }
   w.total = off;
   return w;
 }

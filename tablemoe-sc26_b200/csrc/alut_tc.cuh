@@ -1,22 +1,34 @@
 // Tensor-core centroid scan for large batches (prefill, large tables): tcgen05.
 //
-// Scores of a tile of 128 queries x 128 centroids come from tcgen05.mma (kind::f16, bf16
-// operands, fp32 accumulator in tensor memory) over a two-part bf16 split of both operands:
-//   q . k  ~=  q_hi . k_hi + q_hi . k_lo + q_lo . k_hi      (q_lo = bf16(q - q_hi), same for k)
-// whose error is below delta = 2^-13 |q| max|k| (the split leaves ~2^-16 relative per
-// product; the bound keeps a wide safety factor). The tensor cores therefore only choose
-// candidates: every centroid whose approximate score is within 2*delta of the larger of the
-// tile's approximate best and the slot's current exact best is rescored exactly in fp32 on
-// the CUDA cores and folded into the slot's packed best with atomicMax. The true best always
-// survives the filter (its approximate score is within delta of its exact score, which is
-// at least every other exact score), so the result is the exact fp32 argmax (first index on
-// ties), as on the CUDA-core paths.
+// Scores of a tile of 128 searched slots x 128 centroids come from tcgen05.mma (kind::f16,
+// bf16 operands, fp32 accumulator in tensor memory) of the bf16-rounded query and key:
+//   |q.k - bf16(q).bf16(k)| <= (2 + 2^-9) 2^-9 |q| |k| + (fp32 accumulation) <= delta,
+//   delta = (2^-8 + 2^-11) |q| max|k|       (Cauchy-Schwarz on the two rounding residues).
+// The tensor cores therefore only choose candidates. Each epilogue thread (one slot) keeps
+// the running maximum `amax` of its approximate scores and a short list of the centroids
+// whose approximate score is >= amax - 2 delta; at the end of its slot's range of centroids
+// the survivors are rescored exactly in fp32 (sequential fmaf over l, the summation order
+// of the CUDA-core scans, so the scores are bit-identical to theirs) and folded into the
+// slot's packed best with atomicMax. The true best always survives: its approximate score
+// is within delta of its exact score, which is at least every other exact score. So the
+// result is the exact fp32 argmax (first index on ties: tied centroids all survive), as on
+// the CUDA-core paths. A full list is first pruned, then rescored on the spot.
 //
-// Keys are prepared once (alut_prepare_keys): each table's 128-row chunks as the two bf16
-// parts in the K-major core-matrix order of the tensor-core operand descriptors, so one TMA
-// bulk copy brings a chunk's operand into shared memory; queries are split while being
-// staged. One CTA per SM (persistent over a contiguous range of tiles so that a group's
-// queries are staged once), 128 threads: thread r owns TMEM lane r = query row r.
+// Layout: keys are prepared once (alut_prepare_keys) as bf16 128-row chunks in the K-major,
+// no-swizzle core-matrix order of the tensor-core operand descriptors, followed by each
+// table's largest row norm; the searched slots' queries are staged per search group in the
+// same order (k_stage_queries). One TMA bulk copy then brings a whole operand tile.
+//
+// Pipeline (one CTA per SM, persistent over a contiguous range of (group, chunk) tiles so
+// that a group's query tile is loaded once and its chunks stream in order):
+//   warp 4 (producer): query tile -> A[2], key chunk -> stage ring (mbarrier full/empty);
+//   warp 5 (MMA): allocates 256 TMEM columns, issues L/16 MMAs per tile into one of two
+//                 accumulators, commits to the stage's `empty`, the accumulator's `full`
+//                 and, at a group's last tile, the query buffer's `empty` barrier;
+//   warps 0-3 (epilogue): thread r reads TMEM lane r (slot r of the group), 128 columns,
+//                 releases the accumulator, filters, rescores at the group's end.
+// Every wait is bounded in time; on expiry the CTA records an error bit, stops all roles,
+// drains what it has in flight (bounded), frees TMEM and returns.
 #pragma once
 
 #include "alut_common.cuh"
@@ -24,10 +36,15 @@
 
 namespace alut {
 
-constexpr int kTcRows = 128;   // queries per tile (MMA M) and centroids per chunk (MMA N)
+constexpr int kTcRows = 128;        // slots per tile (MMA M) and centroids per chunk (MMA N)
 constexpr int kTcMaxL = 128;
-constexpr int kTcThreads = 128;
-constexpr int kTcMinPairs = 512;  // below this the CUDA-core scans are used
+constexpr int kTcEpiThreads = 128;  // warps 0-3
+constexpr int kTcThreads = 192;     // + producer warp + MMA warp
+constexpr int kTcMinPairs = 512;    // below this the CUDA-core scans are used
+constexpr int kTcCand = 4;          // candidate list per slot
+constexpr int kTcMaxStages = 8;
+constexpr uint32_t kTcTmemCols = 2 * kTcRows;  // two fp32 128x128 accumulators
+constexpr size_t kTcSmemBudget = 200 * 1024;
 
 // Byte offset of element (row, k) in a [rows][L] bf16 operand in the K-major, no-swizzle
 // core-matrix order: 8-row x 16-byte core matrices, k-chunks adjacent (128 B apart), 8-row
@@ -36,48 +53,112 @@ __host__ __device__ __forceinline__ uint32_t tc_off(int r, int k, int L) {
   return static_cast<uint32_t>((r >> 3) * (L * 16) + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
 }
 
-__host__ __device__ inline size_t tc_chunk_bytes(int l) { return static_cast<size_t>(2) * kTcRows * l * 2; }
+// One operand tile: 128 rows x L bf16.
+__host__ __device__ inline size_t tc_tile_bytes(int l) { return static_cast<size_t>(kTcRows) * l * 2; }
+inline int tc_stages(int l) {
+  const size_t t = tc_tile_bytes(l);
+  const size_t n = (kTcSmemBudget - 1024 - 2 * t - sizeof(float) * 2 * kTcCand * kTcRows) / t;
+  return static_cast<int>(n < kTcMaxStages ? n : kTcMaxStages);
+}
+inline size_t search_tc_smem_bytes(int l) {
+  return 1024 + (2 + static_cast<size_t>(tc_stages(l))) * tc_tile_bytes(l) + sizeof(float) * 2 * kTcCand * kTcRows;
+}
+// Upper bound of the search groups of the tensor-core plan (groups of <= 128 slots of one table).
+__host__ __device__ inline int64_t tc_max_groups(int64_t pairs, int ntab) {
+  return (pairs + kTcRows - 1) / kTcRows + (pairs < ntab ? pairs : ntab) + 1;
+}
 
 // ---- preparation ---------------------------------------------------------------------------
 
-// out: [tables][nchunks][2 parts][128 x L bf16 core-matrix order], then float norms[tables].
+// out: [tables][nchunks][128 x L bf16 core-matrix order], then float norms[tables].
+// One thread per (table, chunk, row, 8 columns): eight reads, one 16-byte store.
 __global__ void k_prepare_keys(const float* keys, int64_t se, int64_t sm, int64_t sk, int ntab, int K, int L,
                                int nchunks, __nv_bfloat16* out, float* norms) {
-  const int64_t per_chunk = static_cast<int64_t>(2) * kTcRows * L;
-  const int64_t total = static_cast<int64_t>(ntab) * nchunks * kTcRows * L;
+  const int units = L / 8;
+  const int64_t total = static_cast<int64_t>(ntab) * nchunks * kTcRows * units;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int k = static_cast<int>(i % L);
-    const int64_t rowg = i / L;  // (table, chunk, row)
+    const int u = static_cast<int>(i % units);
+    const int64_t rowg = i / units;  // (table, chunk, row)
     const int r = static_cast<int>(rowg % kTcRows);
-    const int64_t tc = rowg / kTcRows;
-    const int c = static_cast<int>(tc % nchunks);
-    const int t = static_cast<int>(tc / nchunks);
+    const int64_t tcn = rowg / kTcRows;
+    const int c = static_cast<int>(tcn % nchunks);
+    const int t = static_cast<int>(tcn / nchunks);
     const int kr = c * kTcRows + r;
-    float v = 0.f;
-    if (kr < K) v = keys[static_cast<int64_t>(t >> 1) * se + static_cast<int64_t>(t & 1) * sm + kr * sk + k];
-    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-    const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
-    __nv_bfloat16* base = out + tc * per_chunk;
-    const uint32_t off = tc_off(r, k, L) / 2;
-    base[off] = hi;
-    base[static_cast<int64_t>(kTcRows) * L + off] = lo;
-  }
-  // Largest row norm per table (one warp per table, grid-stride).
-  const int lane = threadIdx.x & 31;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int nw = (gridDim.x * blockDim.x) >> 5;
-  for (int t = gw; t < ntab; t += nw) {
-    float mx = 0.f;
-    const float* tb = keys + static_cast<int64_t>(t >> 1) * se + static_cast<int64_t>(t & 1) * sm;
-    for (int kr = lane; kr < K; kr += 32) {
-      float ss = 0.f;
-      for (int k = 0; k < L; ++k) ss = fmaf(tb[kr * sk + k], tb[kr * sk + k], ss);
-      mx = fmaxf(mx, sqrtf(ss));
-    }
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (kr < K) {
+      const float* src = keys + static_cast<int64_t>(t >> 1) * se + static_cast<int64_t>(t & 1) * sm +
+                         static_cast<int64_t>(kr) * sk + u * 8;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) norms[t] = mx;
+      for (int j = 0; j < 8; ++j) v[j] = src[j];
+    }
+    __align__(16) __nv_bfloat16 h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = __float2bfloat16_rn(v[j]);
+    unsigned char* base = reinterpret_cast<unsigned char*>(out) + tcn * tc_tile_bytes(L);
+    *reinterpret_cast<uint4*>(base + tc_off(r, u * 8, L)) = *reinterpret_cast<const uint4*>(h);
+  }
+  // Largest row norm per table: one thread per (table, row) partial, warp max, atomicMax on
+  // the float bits (norms are >= 0, so their bit patterns order like the values; the output
+  // norms are zeroed by the caller before the launch).
+  const int64_t nrows = static_cast<int64_t>(ntab) * K;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i - (threadIdx.x & 31) < nrows;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float nrm = 0.f;
+    int t = 0;
+    if (i < nrows) {
+      t = static_cast<int>(i / K);
+      const int kr = static_cast<int>(i % K);
+      const float* row = keys + static_cast<int64_t>(t >> 1) * se + static_cast<int64_t>(t & 1) * sm +
+                         static_cast<int64_t>(kr) * sk;
+      float ss = 0.f;
+      for (int k = 0; k < L; ++k) ss = fmaf(row[k], row[k], ss);
+      nrm = sqrtf(ss);
+    }
+    // Lanes of a warp may straddle two tables: reduce per table id.
+    const int t0 = __shfl_sync(0xffffffffu, t, 0);
+    float m0 = t == t0 ? nrm : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+    if ((threadIdx.x & 31) == 0 && i < nrows) atomicMax(reinterpret_cast<int*>(norms + t0), __float_as_int(m0));
+    if (t != t0 && i < nrows) atomicMax(reinterpret_cast<int*>(norms + t), __float_as_int(nrm));
+  }
+}
+
+// The searched slots' queries, per search group of the plan: [groups][128 x L bf16] in the
+// operand order, plus each row's |q| (0 for the padding rows of a partial group).
+// One thread per (group, row, 8 columns).
+__global__ void k_stage_queries(const float* qlow, int L, int s, const int* sorted, const int4* groups,
+                                const int* meta, int64_t max_groups, __nv_bfloat16* qsplit, float* qnorm) {
+  const int units = L / 8;
+  const int64_t ngroups = min(static_cast<int64_t>(meta[0]), max_groups);
+  const int64_t total = ngroups * kTcRows * units;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int u = static_cast<int>(i % units);
+    const int r = static_cast<int>((i / units) % kTcRows);
+    const int64_t g = i / (static_cast<int64_t>(units) * kTcRows);
+    const int4 gg = groups[g];
+    const int p = r < gg.z ? sorted[gg.y + r] : -1;
+    const float* qrow = p >= 0 ? qlow + static_cast<int64_t>(p / s) * L : nullptr;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (qrow) {
+      const float4 a = *reinterpret_cast<const float4*>(qrow + u * 8);
+      const float4 b = *reinterpret_cast<const float4*>(qrow + u * 8 + 4);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    __align__(16) __nv_bfloat16 h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = __float2bfloat16_rn(v[j]);
+    unsigned char* base = reinterpret_cast<unsigned char*>(qsplit) + g * tc_tile_bytes(L);
+    *reinterpret_cast<uint4*>(base + tc_off(r, u * 8, L)) = *reinterpret_cast<const uint4*>(h);
+    if (u == 0) {
+      float ss = 0.f;
+      if (qrow)
+        for (int k = 0; k < L; ++k) ss = fmaf(qrow[k], qrow[k], ss);
+      qnorm[g * kTcRows + r] = sqrtf(ss);
+    }
   }
 }
 
@@ -103,6 +184,11 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t da, uint64_t db, 
       "l"(da), "l"(db), "r"(tc_idesc()), "r"(acc)
       : "memory");
 }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+// Warp-collective (.aligned): every lane of the warp must execute it at the same call site.
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
@@ -119,6 +205,59 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Bounded wait that also gives up when another role of the CTA has aborted.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t n = 0;; ++n) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((n & 15) == 15 && (*abort_flag || global_ns() - t0 > kWaitNs)) return false;
+  }
+}
+
+// Exact fp32 score of one centroid row: sequential fmaf over l (the CUDA-core scans' order).
+__device__ __forceinline__ float tc_exact(const float* q, const float* kp, int L) {
+  float e = 0.f;
+#pragma unroll 4
+  for (int l = 0; l < L; l += 4) {
+    const float4 a = *reinterpret_cast<const float4*>(q + l);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(kp + l));
+    e = fmaf(b.x, a.x, e);
+    e = fmaf(b.y, a.y, e);
+    e = fmaf(b.z, a.z, e);
+    e = fmaf(b.w, a.w, e);
+  }
+  return e;
+}
+
+// A full candidate list (n == kTcCand entries of slot r in s_cc/s_cv): drop the entries that
+// fell below amax - tw; if none did, rescore them all into s_mine[r] and empty the list.
+// Returns the new length. Kept out of line: the filter loop that calls it is unrolled, and
+// this path is rare.
+__device__ __noinline__ int tc_make_room(int r, float amax, float tw, const float* q, const float* kt,
+                                         int64_t sk, int L, uint32_t idx_offset, int* s_cc, float* s_cv,
+                                         unsigned long long* s_mine) {
+  int m = 0;
+  for (int i = 0; i < kTcCand; ++i)
+    if (s_cv[i * kTcRows + r] >= amax - tw) {
+      s_cc[m * kTcRows + r] = s_cc[i * kTcRows + r];
+      s_cv[m * kTcRows + r] = s_cv[i * kTcRows + r];
+      ++m;
+    }
+  if (m < kTcCand) return m;
+  unsigned long long mine = s_mine[r];
+  for (int i = 0; i < kTcCand; ++i) {
+    const int kr = s_cc[i * kTcRows + r];
+    const unsigned long long c = pack_cand(tc_exact(q, kt + static_cast<int64_t>(kr) * sk, L),
+                                           idx_offset + static_cast<uint32_t>(kr));
+    mine = c > mine ? c : mine;
+  }
+  s_mine[r] = mine;
+  return 0;
+}
 
 // ---- scan ------------------------------------------------------------------------------------
 
@@ -127,9 +266,11 @@ struct TcArgs {
   const float* knorm;           // [tables] largest row norm
   const float* keys;            // fp32 keys for the exact rescoring
   int64_t key_stride_e, key_stride_m, key_stride_k;
-  int k, l, s, nchunks;
+  int k, l, s, nchunks, stages;
   uint32_t idx_offset;
   const float* qlow;
+  const unsigned char* qsplit;  // [groups][128 x L bf16]
+  const float* qnorm;           // [groups][128]
   const int* sorted;
   const int4* groups;
   const int* meta;
@@ -137,172 +278,259 @@ struct TcArgs {
   int* err;
 };
 
-inline size_t search_tc_smem_bytes(int l) { return 1024 + 3 * tc_chunk_bytes(l); }  // A + 2 x B
+#ifdef ALUT_PHASE_TRACE
+// Development builds: epilogue thread 0 of block 0 sums its waits for the accumulator (slot
+// 40), its filtering (41) and its rescoring (42) in ns; slot 48 counts rescored centroids.
+#define TC_T0() const uint64_t tc_t0_ = global_ns()
+#define TC_ACC(slot) \
+  if (blockIdx.x == 0 && threadIdx.x == 0) g_alut_trace[slot] += global_ns() - tc_t0_
+#define TC_COUNT() \
+  if (blockIdx.x == 0) atomicAdd(&g_alut_trace[48], 1ull)
+#else
+#define TC_T0() do {} while (0)
+#define TC_ACC(slot) do {} while (0)
+#define TC_COUNT() do {} while (0)
+#endif
 
 __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
   extern __shared__ __align__(1024) unsigned char tsm[];
   const int L = a.l;
-  const size_t cb = tc_chunk_bytes(L);
-  unsigned char* sA = tsm + 1024;                         // [2 parts][128 x L] queries
-  unsigned char* sB = sA + cb;                            // [2 buffers][2 parts][128 x L] keys
-  uint64_t* bar = reinterpret_cast<uint64_t*>(tsm);       // [0],[1] key buffers, [2] MMA done
+  const int NS = a.stages;
+  const uint32_t tb = static_cast<uint32_t>(tc_tile_bytes(L));
+  uint64_t* full = reinterpret_cast<uint64_t*>(tsm);  // [kTcMaxStages]
+  uint64_t* empty = full + kTcMaxStages;              // [kTcMaxStages]
+  uint64_t* a_full = empty + kTcMaxStages;            // [2] query tiles
+  uint64_t* a_empty = a_full + 2;                     // [2]
+  uint64_t* t_full = a_empty + 2;                     // [2] accumulators
+  uint64_t* t_empty = t_full + 2;                     // [2]
+  uint64_t* drain = t_empty + 2;                      // [1]
+  unsigned char* sA = tsm + 1024;                     // [2][tile]
+  unsigned char* sK = sA + 2 * tb;                    // [NS][tile]
+  int* s_cc = reinterpret_cast<int*>(sK + static_cast<size_t>(NS) * tb);  // [kTcCand][128]
+  float* s_cv = reinterpret_cast<float*>(s_cc + kTcCand * kTcRows);       // [kTcCand][128]
+  __shared__ unsigned long long s_mine[kTcRows];  // slot r's best exactly rescored candidate
   __shared__ uint32_t s_tmem;
-  __shared__ int pid[kTcRows];
-  __shared__ float s_qn[kTcRows];
-  __shared__ int s_abort;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  __shared__ int s_abort, s_issued, s_groups_issued;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  volatile int* abort_flag = &s_abort;
+
   const int ntiles = a.meta[0] * a.nchunks;
   const int t_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * ntiles / gridDim.x);
   const int t_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * ntiles / gridDim.x);
   if (t_begin >= t_end) return;
-  if (warp == 0) {
+  if (warp == 5) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
-                 "r"(kTcRows)
+                 "r"(kTcTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
+    for (int i = 0; i < kTcMaxStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&a_full[i], 1);
+      mbar_init(&a_empty[i], 1);
+      mbar_init(&t_full[i], 1);
+      mbar_init(&t_empty[i], kTcEpiThreads / 32);
+    }
+    mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_abort = 0;
+    s_issued = 0;
+    s_groups_issued = 0;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
-  auto issue_b = [&](int tile, int b) {  // thread 0
-    const int4 g = a.groups[tile / a.nchunks];
-    const int chunk = tile % a.nchunks;
-    const unsigned char* src = a.ksplit + (static_cast<int64_t>(g.x) * a.nchunks + chunk) * cb;
-    fence_async_shared();
-    mbar_expect_tx(&bar[b], static_cast<uint32_t>(cb));
-    bulk_g2s(sB + b * cb, src, static_cast<uint32_t>(cb), &bar[b]);
-  };
-  if (tid == 0) issue_b(t_begin, 0);
-  int cur_group = -1, table = 0, cnt = 0;
-  float qn = 0.f;
-  int it = 0;
-  for (int tile = t_begin; tile < t_end; ++tile, ++it) {
-    const int b = it & 1;
-    const int g = tile / a.nchunks, chunk = tile % a.nchunks;
-    if (tid == 0 && tile + 1 < t_end) issue_b(tile + 1, b ^ 1);  // that buffer's MMAs finished last iteration
-    if (g != cur_group) {
-      const int4 gg = a.groups[g];
-      table = gg.x;
-      cnt = gg.z;
-      cur_group = g;
-      // Stage the group's queries: thread r splits query r into (hi, lo) bf16 parts.
-      const int r = tid;
-      float ss = 0.f;
-      int p = -1;
-      if (r < cnt) p = a.sorted[gg.y + r];
-      pid[r] = p;
-      const float* q = p >= 0 ? a.qlow + static_cast<int64_t>(p / a.s) * L : nullptr;
-      for (int k = 0; k < L; ++k) {
-        const float v = q ? q[k] : 0.f;
-        ss = fmaf(v, v, ss);
-        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-        const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
-        const uint32_t off = tc_off(r, k, L);
-        *reinterpret_cast<__nv_bfloat16*>(sA + off) = hi;
-        *reinterpret_cast<__nv_bfloat16*>(sA + cb / 2 + off) = lo;
+
+  if (warp == 4) {
+    // ---- producer --------------------------------------------------------------------------
+    if (lane == 0) {
+      int gi = -1, prev = -1, it = 0;
+      bool ok = true;
+      for (int tile = t_begin; tile < t_end && ok; ++tile, ++it) {
+        const int g = tile / a.nchunks, c = tile % a.nchunks;
+        if (g != prev) {
+          const int ab = (gi + 1) & 1;
+          if (gi + 1 >= 2 && !tc_wait(&a_empty[ab], (((gi + 1) >> 1) - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          prev = g;
+          ++gi;
+          mbar_expect_tx(&a_full[ab], tb);
+          bulk_g2s(sA + ab * tb, a.qsplit + static_cast<int64_t>(g) * tb, tb, &a_full[ab]);
+        }
+        const int st = it % NS;
+        if (it >= NS && !tc_wait(&empty[st], ((it / NS) - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int table = a.groups[g].x;
+        mbar_expect_tx(&full[st], tb);
+        bulk_g2s(sK + st * tb, a.ksplit + (static_cast<int64_t>(table) * a.nchunks + c) * tb, tb, &full[st]);
       }
-      s_qn[r] = sqrtf(ss);
-      qn = s_qn[r];
-      fence_async_shared();  // generic-proxy writes of A, visible to the tensor cores
-    }
-    if (tid == 0 && !mbar_wait_bounded(&bar[b], (it >> 1) & 1)) {
-      s_abort = 1;  // keys of this tile (and the next, if issued) may still be in flight
-      atomicOr(a.err, 8);
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (s_abort) break;
-    if (tid == 0) {
-      const uint32_t a0 = smem_addr(sA), b0 = smem_addr(sB + b * cb);
-      const uint32_t half = static_cast<uint32_t>(cb / 2);
-      int n = 0;
-      for (int ks = 0; ks < L / 16; ++ks) {
-        const uint32_t o = ks * 256;
-        tc_mma(tmem, tc_desc(a0 + o, L), tc_desc(b0 + o, L), n++ > 0);                // hi . hi
-        tc_mma(tmem, tc_desc(a0 + o, L), tc_desc(b0 + half + o, L), 1);               // hi . lo
-        tc_mma(tmem, tc_desc(a0 + half + o, L), tc_desc(b0 + o, L), 1);               // lo . hi
-      }
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                       smem_addr(&bar[2]))
-                   : "memory");
-      if (!mbar_wait_bounded(&bar[2], it & 1)) {
-        s_abort = 2;  // the MMAs of this tile may still be running
+      s_issued = it;
+      s_groups_issued = gi + 1;
+      if (!ok && !*abort_flag) {
+        *abort_flag = 1;
         atomicOr(a.err, 8);
       }
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (s_abort) break;
-    // Epilogue: thread r = query r of the group. tcgen05.ld is warp-collective (.aligned):
-    // every load is issued from one call site by the whole, re-converged warp.
-    const int r = tid;
-    const int rows = min(kTcRows, a.k - chunk * kTcRows);
-    const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    float m = -INFINITY;
-    for (int c0 = 0; c0 < kTcRows; c0 += 32) {
-      float v[32];
-      __syncwarp();
-      tc_ld32(taddr + c0, v);
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c0 + j < rows) m = fmaxf(m, v[j]);
-    }
-    const int p = pid[r];
-    float thr = INFINITY;
-    const float* q = nullptr;
-    const float* kt = nullptr;
-    if (p >= 0) {
-      const uint64_t gb = __ldcg(reinterpret_cast<const unsigned long long*>(a.best) + p);
-      const float gs = gb ? cand_score(gb) : -INFINITY;
-      const float delta = 0x1p-13f * qn * a.knorm[table];
-      thr = fmaxf(m, gs) - 2.f * delta;
-      q = a.qlow + static_cast<int64_t>(p / a.s) * L;
-      kt = a.keys + static_cast<int64_t>(table >> 1) * a.key_stride_e + static_cast<int64_t>(table & 1) * a.key_stride_m;
-    }
-    uint64_t mine = 0ull;
-    for (int c0 = 0; c0 < kTcRows; c0 += 32) {
-      float v[32];
-      __syncwarp();
-      tc_ld32(taddr + c0, v);
-      if (p < 0) continue;
-#pragma unroll 1
-      for (int j = 0; j < 32; ++j) {
-        const int col = c0 + j;
-        if (col < rows && v[j] >= thr) {
-          const int kr = chunk * kTcRows + col;
-          const float* kp = kt + static_cast<int64_t>(kr) * a.key_stride_k;
-          float e = 0.f;
-          for (int l = 0; l < L; ++l) e = fmaf(q[l], kp[l], e);
-          const uint64_t c = pack_cand(e, a.idx_offset + static_cast<uint32_t>(kr));
-          mine = c > mine ? c : mine;
+  } else if (warp == 5) {
+    // ---- MMA issuer ------------------------------------------------------------------------
+    if (lane == 0) {
+      int gi = -1, prev = -1, it = 0;
+      bool ok = true;
+      for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+        const int g = tile / a.nchunks;
+        if (g != prev) {
+          prev = g;
+          ++gi;
+          if (!tc_wait(&a_full[gi & 1], (gi >> 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
         }
+        const int st = it % NS, acc = it & 1;
+        if (!tc_wait(&full[st], (it / NS) & 1, abort_flag) ||
+            (it >= 2 && !tc_wait(&t_empty[acc], ((it >> 1) - 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_addr(sA + (gi & 1) * tb), b0 = smem_addr(sK + st * tb);
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * kTcRows);
+        for (int ks = 0; ks < L / 16; ++ks)
+          tc_mma(d, tc_desc(a0 + ks * 256, L), tc_desc(b0 + ks * 256, L), ks > 0);
+        tc_commit(&empty[st]);
+        tc_commit(&t_full[acc]);
+        if (tile + 1 == t_end || (tile + 1) / a.nchunks != g) tc_commit(&a_empty[gi & 1]);
+      }
+      if (!ok && !*abort_flag) {
+        *abort_flag = 1;
+        atomicOr(a.err, 8);
       }
     }
-    if (mine) atomicMax(reinterpret_cast<unsigned long long*>(a.best + p), static_cast<unsigned long long>(mine));
-    __syncwarp();
-    tc_fence_before();
-    __syncthreads();  // TMEM, A and this key buffer are free again
-    tc_fence_after();
+  } else {
+    // ---- epilogue: thread r = slot r of the group ---------------------------------------------
+    const int r = tid;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    int prev = -1, p = -1, n = 0, it = 0;
+    float amax = -INFINITY, tw = 0.f;
+    const float* q = nullptr;
+    const float* kt = nullptr;
+    for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+      const int g = tile / a.nchunks, c = tile % a.nchunks;
+      if (g != prev) {
+        prev = g;
+        const int4 gg = a.groups[g];
+        const int table = gg.x;
+        p = r < gg.z ? a.sorted[gg.y + r] : -1;
+        n = 0;
+        s_mine[r] = 0ull;
+        amax = -INFINITY;
+        if (p >= 0) {
+          const float delta = (0x1p-8f + 0x1p-11f) * a.qnorm[static_cast<int64_t>(g) * kTcRows + r] * a.knorm[table];
+          tw = 2.f * delta;
+          q = a.qlow + static_cast<int64_t>(p / a.s) * L;
+          kt = a.keys + static_cast<int64_t>(table >> 1) * a.key_stride_e +
+               static_cast<int64_t>(table & 1) * a.key_stride_m;
+        }
+      }
+      const int acc = it & 1;
+      bool ok;
+      {
+        TC_T0();
+        ok = tc_wait(&t_full[acc], (it >> 1) & 1, abort_flag);
+        TC_ACC(40);
+      }
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0 && !*abort_flag) {
+          *abort_flag = 1;
+          atomicOr(a.err, 8);
+        }
+        break;
+      }
+      tc_fence_after();
+      {
+        TC_T0();
+        const int rows = min(kTcRows, a.k - c * kTcRows);
+        const int kb = c * kTcRows;
+        for (int c0 = 0; c0 < kTcRows; c0 += 32) {
+          float v[32];
+          __syncwarp();
+          tc_ld32(lane_base + static_cast<uint32_t>(acc * kTcRows + c0), v);
+          if (p < 0) continue;
+          if (c0 + 32 > rows) {  // ragged last chunk
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (c0 + j >= rows) v[j] = -INFINITY;
+          }
+          float m32 = v[0];
+#pragma unroll
+          for (int j = 1; j < 32; ++j) m32 = fmaxf(m32, v[j]);
+          if (!(m32 >= amax - tw)) continue;  // nothing in these 32 columns can be the best
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (v[j] >= amax - tw) {
+              amax = fmaxf(amax, v[j]);
+              if (n == kTcCand)
+                n = tc_make_room(r, amax, tw, q, kt, a.key_stride_k, L, a.idx_offset, s_cc, s_cv, s_mine);
+              s_cc[n * kTcRows + r] = kb + c0 + j;
+              s_cv[n * kTcRows + r] = v[j];
+              ++n;
+            }
+          }
+        }
+        TC_ACC(41);
+      }
+      // This accumulator may be overwritten now.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&t_empty[acc]);
+      if (p >= 0 && (tile + 1 == t_end || (tile + 1) / a.nchunks != g)) {
+        TC_T0();
+        unsigned long long mine = s_mine[r];
+        for (int i = 0; i < n; ++i) {
+          if (s_cv[i * kTcRows + r] < amax - tw) continue;
+          const int kr = s_cc[i * kTcRows + r];
+          const unsigned long long cand = pack_cand(tc_exact(q, kt + static_cast<int64_t>(kr) * a.key_stride_k, L),
+                                                    a.idx_offset + static_cast<uint32_t>(kr));
+          TC_COUNT();
+          mine = cand > mine ? cand : mine;
+        }
+        n = 0;
+        if (mine) atomicMax(reinterpret_cast<unsigned long long*>(a.best + p), static_cast<unsigned long long>(mine));
+        TC_ACC(42);
+      }
+    }
   }
-  // After an abort at iteration `it`, give what this CTA still has in flight (the MMAs, this
-  // tile's key copy, the next tile's key copy) a bounded chance to finish before TMEM is freed.
-  if (s_abort && tid == 0) {
-    const int tile = t_begin + it;
-    if (s_abort == 2) mbar_wait_bounded(&bar[2], it & 1);
-    if (s_abort == 1) mbar_wait_bounded(&bar[it & 1], (it >> 1) & 1);
-    if (tile + 1 < t_end) mbar_wait_bounded(&bar[(it + 1) & 1], ((it + 1) >> 1) & 1);
+
+  __syncthreads();
+  if (*abort_flag && tid == 32 * 5) {
+    // The MMAs this thread issued: a commit after them, waited (bounded).
+    tc_commit(drain);
+    mbar_wait_bounded(drain, 0);
+  }
+  if (*abort_flag && tid == 32 * 4) {
+    // Every copy this CTA issued: the latest use of each stage and query buffer (bounded).
+    const int issued = s_issued, gissued = s_groups_issued;
+    for (int st = 0; st < NS && st < issued; ++st) {
+      const int last = st + ((issued - 1 - st) / NS) * NS;
+      mbar_wait_bounded(&full[st], (last / NS) & 1);
+    }
+    for (int ab = 0; ab < 2 && ab < gissued; ++ab) {
+      const int last = ab + ((gissued - 1 - ab) / 2) * 2;
+      mbar_wait_bounded(&a_full[ab], (last >> 1) & 1);
+    }
   }
   __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcRows) : "memory");
+  if (warp == 5)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
 }
 
 }  // namespace alut
