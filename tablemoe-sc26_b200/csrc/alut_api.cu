@@ -267,7 +267,29 @@ static int launch_project(int key_dtype, int x_dtype, const ProjPlanArgs& a, cud
   return fail(ALUT_EDTYPE, "key dtype");
 }
 
-static int launch_plan(const ProjPlanArgs& a, cudaStream_t st) {
+// Slots above which the plan runs over the whole GPU (three launches) instead of one CTA.
+constexpr int64_t kPlanWideSlots = 4096;
+
+static int launch_plan(const ProjPlanArgs& a, int* tabs, cudaStream_t st) {
+  const int ntab = 2 * a.num_experts;
+  const int64_t pairs = static_cast<int64_t>(a.q) * a.s;
+  if (pairs > kPlanWideSlots) {
+    cudaError_t e = cudaMemsetAsync(tabs, 0, sizeof(int) * ntab, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(a.meta + 1, 0, sizeof(int), st);
+    if (e != cudaSuccess) return fail(ALUT_ECUDA, "plan: %s", cudaGetErrorString(e));
+    const int grid = static_cast<int>(std::min<int64_t>((pairs + 255) / 256, static_cast<int64_t>(num_sms()) * 4));
+    const size_t hs = sizeof(int) * ntab;
+    int rc = allow_smem(reinterpret_cast<const void*>(k_plan_count), hs);
+    if (rc) return rc;
+    k_plan_count<<<grid, 256, hs, st>>>(a, tabs);
+    rc = check_launch("k_plan_count");
+    if (rc) return rc;
+    k_plan_groups<<<1, kProjThreads, 0, st>>>(a, tabs, tabs + ntab);
+    rc = check_launch("k_plan_groups");
+    if (rc) return rc;
+    k_plan_scatter<<<grid, 256, 0, st>>>(a, tabs + ntab);
+    return check_launch("k_plan_scatter");
+  }
   const size_t smem = plan_smem_bytes(2 * a.num_experts);
   int rc = allow_smem(reinterpret_cast<const void*>(k_plan), smem);
   if (rc) return rc;
@@ -438,7 +460,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
   const Workspace wt = workspace_layout(b->q, b->s, t->l, 2 * t->num_experts, true);
   if (ksplit && tc_tables_ok(t) && vec && pairs >= kTcMinPairs && ws_bytes >= wt.total) {
     a.group = kTcRows;
-    int rc = launch_plan(a, st);
+    int rc = launch_plan(a, reinterpret_cast<int*>(base + w.tabs), st);
     if (rc) return rc;
     rc = launch_project(t->key_dtype, b->x_dtype, a, st);
     if (rc) return rc;
@@ -485,7 +507,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     if (g_prof_start && g_prof_stop && record_profile(g_prof_stop, st)) return ALUT_ECUDA;
     return ALUT_OK;
   }
-  int rc = launch_plan(a, st);
+  int rc = launch_plan(a, reinterpret_cast<int*>(base + w.tabs), st);
   if (rc) return rc;
   rc = launch_project(t->key_dtype, b->x_dtype, a, st);
   if (rc) return rc;

@@ -203,6 +203,7 @@ struct Workspace {
   size_t best;      // uint64 [Q * S]        packed best candidate per slot
   size_t sorted;    // int32  [Q * S]        slot ids sorted by table
   size_t groups;    // int4   [max_groups]   (table, first sorted slot, count, 0)
+  size_t tabs;      // int32  [2 * tables]   per-table slot counts, bucket cursors (large plan)
   // Tensor-core scan only (workspace_layout(..., tc = true)): the searched slots' queries
   // staged per group of <= 128 slots as bf16 operand tiles, and their norms.
   size_t qsplit;    // bf16   [tc_groups][128 * L]
@@ -241,6 +242,7 @@ inline Workspace workspace_layout(int q, int s, int l, int num_tables, bool tc =
   w.best = off;     off = align256(off + sizeof(uint64_t) * (pairs + 1));
   w.sorted = off;   off = align256(off + sizeof(int32_t) * (pairs + 1));
   w.groups = off;   off = align256(off + sizeof(int4) * w.max_groups);
+  w.tabs = off;     off = align256(off + sizeof(int32_t) * 2 * num_tables);
   if (tc) {
     // Groups of <= 128 slots of one table (this bound is below max_groups, which the plan's
     // group list uses in both cases).

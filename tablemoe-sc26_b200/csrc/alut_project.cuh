@@ -161,6 +161,97 @@ __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
   }
 }
 
+// ---- plan of large batches: three launches over the whole GPU ----------------------------
+// k_plan serialises every slot through one CTA; for large batches the same plan is built by
+// (1) k_plan_count: clears `best`, counts the searched slots per table (warp-aggregated
+//     shared-memory histogram, one global add per table per CTA), flags bad expert ids;
+// (2) k_plan_groups (one CTA): scans the counts into bucket offsets and the group list;
+// (3) k_plan_scatter: writes each searched slot id into its table's bucket (warp-aggregated
+//     atomics on the bucket cursors). The order inside a bucket does not matter.
+// `counts` must be zero before (1); meta[1] (error bits) likewise.
+
+// Table of slot p, or -1 when the slot is not searched (reuse mask off) or its expert id is
+// out of range (then *bad is set).
+__device__ __forceinline__ int plan_table(const ProjPlanArgs& a, int64_t p, bool* bad) {
+  const int qq = static_cast<int>(p / a.s), ss = static_cast<int>(p % a.s);
+  const bool r = a.reuse ? (a.reuse[qq * a.reuse_stride + ss] != 0) : true;
+  if (!r) return -1;
+  const int64_t e = a.sel[qq * a.sel_stride + ss];
+  if (e < 0 || e >= a.num_experts) {
+    *bad = true;
+    return -1;
+  }
+  return static_cast<int>(e) * 2 + (a.is_vision[qq] ? 0 : 1);
+}
+
+__global__ void __launch_bounds__(256) k_plan_count(ProjPlanArgs a, int* counts) {
+  extern __shared__ __align__(16) int hist[];
+  const int ntab = 2 * a.num_experts;
+  const int64_t pairs = static_cast<int64_t>(a.q) * a.s;
+  for (int t = threadIdx.x; t < ntab; t += blockDim.x) hist[t] = 0;
+  __syncthreads();
+  bool bad = false;
+  const int lane = threadIdx.x & 31;
+  for (int64_t base = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) - lane; base < pairs;
+       base += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t p = base + lane;
+    int t = -1;
+    if (p < pairs) {
+      a.best[p] = 0ull;
+      t = plan_table(a, p, &bad);
+    }
+    const unsigned same = __match_any_sync(0xffffffffu, t);
+    if (t >= 0 && lane == __ffs(same) - 1) atomicAdd(&hist[t], __popc(same));
+  }
+  if (bad) atomicOr(&a.meta[1], 1);
+  __syncthreads();
+  for (int t = threadIdx.x; t < ntab; t += blockDim.x)
+    if (hist[t]) atomicAdd(&counts[t], hist[t]);
+}
+
+__global__ void __launch_bounds__(kProjThreads) k_plan_groups(ProjPlanArgs a, const int* counts, int* offs) {
+  const int tid = threadIdx.x;
+  const int G = a.group > 0 ? a.group : kSearchGroup;
+  const int ntab = 2 * a.num_experts;
+  __shared__ int scan_scratch[kProjThreads];
+  __shared__ int s_tot_c, s_tot_g;
+  const int per = (ntab + kProjThreads - 1) / kProjThreads;
+  const int t0 = tid * per;
+  const int t1 = min(ntab, t0 + per);
+  int lc = 0, lg = 0;
+  for (int t = t0; t < t1; ++t) {
+    lc += counts[t];
+    lg += (counts[t] + G - 1) / G;
+  }
+  int bc = block_exclusive_scan_256(lc, scan_scratch, &s_tot_c);
+  int bg = block_exclusive_scan_256(lg, scan_scratch, &s_tot_g);
+  for (int t = t0; t < t1; ++t) {
+    offs[t] = bc;
+    const int c = counts[t];
+    for (int g = 0; g * G < c; ++g) a.groups[bg + g] = make_int4(t, bc + g * G, min(G, c - g * G), 0);
+    bc += c;
+    bg += (c + G - 1) / G;
+  }
+  if (tid == 0) a.meta[0] = s_tot_g;
+}
+
+__global__ void __launch_bounds__(256) k_plan_scatter(ProjPlanArgs a, int* offs) {
+  const int64_t pairs = static_cast<int64_t>(a.q) * a.s;
+  const int lane = threadIdx.x & 31;
+  bool bad = false;
+  for (int64_t base = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) - lane; base < pairs;
+       base += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t p = base + lane;
+    const int t = p < pairs ? plan_table(a, p, &bad) : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, t);
+    const int leader = __ffs(same) - 1;
+    int pos = 0;
+    if (t >= 0 && lane == leader) pos = atomicAdd(&offs[t], __popc(same));
+    pos = __shfl_sync(0xffffffffu, pos, leader);
+    if (t >= 0) a.sorted[pos + __popc(same & ((1u << lane) - 1))] = static_cast<int>(p);
+  }
+}
+
 // ---- projection ---------------------------------------------------------------------------
 
 // Bias, rounding to the key dtype and optional L2 normalisation of rows [r0, r1) of a
