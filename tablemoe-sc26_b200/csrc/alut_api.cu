@@ -12,6 +12,7 @@
 #include "alut_project.cuh"
 #include "alut_search.cuh"
 #include "alut_tc.cuh"
+#include "alut_project_tc.cuh"
 
 namespace alut {
 
@@ -86,6 +87,8 @@ static int allow_smem(const void* kernel, size_t bytes) {
   if (used < 256) table[used++] = Entry{kernel, dev, static_cast<int>(bytes)};
   return ALUT_OK;
 }
+
+static size_t basis_plain_bytes(int l, int h) { return static_cast<size_t>(2) * 3 * l * h * sizeof(__nv_bfloat16); }
 
 // Tables whose keys the tensor-core scan can take (once their bf16 form is prepared).
 static bool tc_tables_ok(const alut_tables_t* t) {
@@ -253,6 +256,34 @@ static bool mma_projection_ok(int key_dtype, int x_dtype, const ProjPlanArgs& a)
 
 static int launch_project(int key_dtype, int x_dtype, const ProjPlanArgs& a, cudaStream_t st) {
   const size_t smem = proj_smem_bytes(a.l);
+  if (mma_projection_ok(key_dtype, x_dtype, a) && a.q >= kPtMinTokens && pt_shape_ok(a.l, a.h) &&
+      a.x_stride % 8 == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && a.zero_best == nullptr && a.meta) {
+    // Large batch: tcgen05 projection over 128-token tiles (the basis's operand-order copy
+    // follows the plain split, see alut_prepare_basis).
+    PtArgs p{};
+    p.x = static_cast<const __nv_bfloat16*>(a.x);
+    p.x_stride = a.x_stride;
+    p.is_vision = a.is_vision;
+    p.basis = reinterpret_cast<const unsigned char*>(a.proj_split) + align256(basis_plain_bytes(a.l, a.h));
+    p.bias[0] = static_cast<const float*>(a.bias[0]);
+    p.bias[1] = static_cast<const float*>(a.bias[1]);
+    p.q = a.q;
+    p.h = a.h;
+    p.l = a.l;
+    p.stages = pt_stages(a.l);
+    p.normalize = a.normalize;
+    p.eps = a.eps;
+    p.qlow = a.qlow;
+    p.q_out = static_cast<float*>(a.q_out);
+    p.q_out_stride = a.q_out_stride;
+    p.err = a.meta + 1;
+    const size_t sm = pt_smem_bytes(a.l);
+    int rc = allow_smem(reinterpret_cast<const void*>(k_project_tc), sm);
+    if (rc) return rc;
+    const int ntiles = ceil_div(a.q, kTcRows);
+    k_project_tc<<<std::min(ntiles, num_sms()), kPtThreads, sm, st>>>(p);
+    return check_launch("k_project_tc");
+  }
   if (mma_projection_ok(key_dtype, x_dtype, a)) {
     // The cluster size may drop to 8 inside launch_project_kernel; size for the larger layout.
     const size_t sm = std::max(mma_smem_layout(a.l, a.h, a.nsplit).total,
@@ -609,9 +640,13 @@ int alut_prepare_keys(const alut_tables_t* t, int32_t keyset, void* out, size_t 
   return check_launch("k_prepare_keys");
 }
 
+// Plain split [2][3][L][H] (decode-shaped projection), then, when the shape allows the
+// large-batch tensor-core projection, the same parts in its operand order.
+
 size_t alut_basis_split_bytes(const alut_tables_t* t) {
   if (!t || t->proj_dtype != ALUT_F32 || t->h <= 0 || t->l <= 0 || t->h % 16 != 0 || t->l % 8 != 0) return 0;
-  return static_cast<size_t>(2) * 3 * t->l * t->h * sizeof(__nv_bfloat16);
+  const size_t plain = basis_plain_bytes(t->l, t->h);
+  return pt_shape_ok(t->l, t->h) ? align256(plain) + pt_basis_bytes(t->l, t->h) : plain;
 }
 
 int alut_prepare_basis(const alut_tables_t* t, void* out, size_t out_bytes, alut_stream_t stream) {
@@ -622,7 +657,12 @@ int alut_prepare_basis(const alut_tables_t* t, void* out, size_t out_bytes, alut
   k_split_basis<<<592, kProjThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const float*>(t->proj[0]), static_cast<const float*>(t->proj[1]), t->proj_stride_h, t->h, t->l,
       static_cast<__nv_bfloat16*>(out));
-  return check_launch("k_split_basis");
+  int rc = check_launch("k_split_basis");
+  if (rc || !pt_shape_ok(t->l, t->h)) return rc;
+  k_split_basis_tc<<<592, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const float*>(t->proj[0]), static_cast<const float*>(t->proj[1]), t->proj_stride_h, t->h, t->l,
+      reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(out) + align256(basis_plain_bytes(t->l, t->h))));
+  return check_launch("k_split_basis_tc");
 }
 
 size_t alut_workspace_size(const alut_tables_t* tables, int32_t q, int32_t s) {
@@ -667,6 +707,7 @@ int alut_project(const alut_tables_t* tables, const alut_batch_t* batch, int32_t
   a.qlow = reinterpret_cast<float*>(base + w.qlow);
   a.q_out = q_low;
   a.q_out_stride = q_low_stride;
+  a.meta = reinterpret_cast<int*>(base + w.meta);
   return launch_project(tables->key_dtype, batch->x_dtype, a, reinterpret_cast<cudaStream_t>(stream));
 }
 

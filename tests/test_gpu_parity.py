@@ -220,6 +220,63 @@ def test_projection_matches_oracle():
         assert np.all(np.abs(q.cpu().numpy() - ref) <= tol)
 
 
+@pytest.mark.parametrize("Q,H,L,vis,normalize", [
+    (1000, 2048, 64, "mixed", False),    # tiles holding both modalities
+    (4096, 2048, 64, "first1024", True),  # C3-like: image tokens first, pure tiles
+    (300, 512, 128, "mixed", True),      # ragged last tile, L = 128
+    (777, 256, 48, "none", False),       # L = 48, text only
+])
+def test_large_batch_projection_matches_oracle(Q, H, L, vis, normalize):
+    """bf16 tokens, fp32 basis, >= 256 tokens: the tcgen05 projection (128-token tiles, basis
+    in three bf16 parts); q within fp32 accuracy of the oracle."""
+    g = torch.Generator().manual_seed(Q + L)
+    x = torch.randn(Q, H, generator=g).to(torch.bfloat16)
+    is_vis = {"mixed": torch.rand(Q, generator=g) < 0.5, "none": torch.zeros(Q, dtype=torch.bool),
+              "first1024": torch.arange(Q) < 1024}[vis]
+    proj = torch.stack([torch.linalg.qr(torch.randn(H, L, generator=g))[0] for _ in range(2)]).contiguous()
+    bias = torch.randn(2, L, generator=g) * 0.1
+    raw = torch.randn(2, 2, 16, L, generator=g)
+    pca = {m: {"proj": proj[i].to(DEV), "bias": bias[i].to(DEV)} for i, m in enumerate(("vision", "text"))}
+    values = torch.zeros(2, 2, 16, H, dtype=torch.bfloat16, device=DEV)
+    mgr = HybridStorageManager.from_tables(0, raw.to(DEV), values, pca)
+    lib = _alut.load()
+    t = mgr.alut_tables()
+    xb, visb, selb = x.to(DEV), is_vis.to(DEV), torch.zeros(Q, 1, dtype=torch.long, device=DEV)
+    b = _alut.make_batch(xb, selb, visb, None)
+    ws = torch.zeros(lib.alut_workspace_size(t, Q, 1), dtype=torch.uint8, device=DEV)
+    q = torch.full((Q, L), float("nan"), device=DEV)
+    _alut.check(lib.alut_project(t, ctypes.byref(b), int(normalize), 1e-6, q.data_ptr(), L, ws.data_ptr(), ws.numel(),
+                                 _alut.stream_ptr(DEV)), "alut_project")
+    ref = orc.project(x.float().numpy(), is_vis.numpy(), proj.numpy(), bias.numpy(), normalize=normalize)
+    bound = np.abs(x.float().numpy()).sum(axis=1, keepdims=True) * float(np.abs(proj.numpy()).max())
+    tol = (1e-5 if normalize else 1e-6 * bound) + 1e-6
+    got = q.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert np.all(np.abs(got - ref) <= tol), float(np.max(np.abs(got - ref) - tol))
+
+
+def test_large_batch_cosine_search_bf16_tokens():
+    """search_prefill_offline (normalised queries, cosine keys) with bf16 tokens at prefill
+    size: tcgen05 projection + tensor-core scan against the oracle."""
+    s = synth(Q=1024, S=4, E=8, K=512, L=64, H=1024, seed=21, vis_frac=0.3, reuse_p=0.6)
+    q0 = orc.project(s["x"].float().numpy(), s["vis"].numpy(), s["proj"].float().numpy(), s["bias"].float().numpy())
+    for t in range(64):  # planted hits: a key along the token's own query, per routed slot
+        m = 0 if bool(s["vis"][t]) else 1
+        for j in range(4):
+            s["raw"][int(s["sel"][t, j]), m, 100 + t] = torch.from_numpy(q0[t]) * 2
+    mgr = synth_manager(s)
+    eng = VectorSearchEngine(mgr)
+    hit, idx = eng.search_prefill_offline(0, s["x"].to(DEV), s["sel"].to(DEV), s["vis"].to(DEV), s["reuse"].to(DEV))
+    q = orc.project(s["x"].float().numpy(), s["vis"].numpy(), s["proj"].float().numpy(), s["bias"].float().numpy(),
+                    normalize=True)
+    keys = mgr.keys_buffer.cpu().numpy()
+    rh, ri, _, _ = orc.search(q, keys, s["sel"].numpy(), s["vis"].numpy(), s["reuse"].numpy(), 0.6, 0.7, cmp_ge=True)
+    check_search(hit.cpu().numpy(), idx.cpu().numpy(), rh, ri, q, keys, s["sel"].numpy(), s["vis"].numpy(),
+                 (0.6, 0.7), "float32", what="cos bf16")
+    assert mgr._keys_split.get(_alut.KEYS_NORMALISED) is not None
+    assert rh[:64][s["reuse"].numpy()[:64]].all()
+
+
 @pytest.mark.parametrize("kdt", ["bfloat16", "float16"])
 def test_16bit_tables_match_oracle(kdt):
     dt = TDT[kdt]
