@@ -38,8 +38,9 @@ namespace alut {
 
 constexpr int kTcRows = 128;        // slots per tile (MMA M) and centroids per chunk (MMA N)
 constexpr int kTcMaxL = 128;
-constexpr int kTcEpiThreads = 128;  // warps 0-3
-constexpr int kTcThreads = 192;     // + producer warp + MMA warp
+constexpr int kTcEpiThreads = 256;  // warps 0-7: (TMEM lane quarter, column half)
+constexpr int kTcThreads = 320;     // + producer warp 8 + MMA warp 9
+constexpr int kTcProducerWarp = 8, kTcMmaWarp = 9;
 constexpr int kTcMinPairs = 512;    // below this the CUDA-core scans are used
 constexpr int kTcCand = 4;          // candidate list per slot
 constexpr int kTcMaxStages = 8;
@@ -57,11 +58,12 @@ __host__ __device__ __forceinline__ uint32_t tc_off(int r, int k, int L) {
 __host__ __device__ inline size_t tc_tile_bytes(int l) { return static_cast<size_t>(kTcRows) * l * 2; }
 inline int tc_stages(int l) {
   const size_t t = tc_tile_bytes(l);
-  const size_t n = (kTcSmemBudget - 1024 - 2 * t - sizeof(float) * 2 * kTcCand * kTcRows) / t;
+  const size_t n = (kTcSmemBudget - 1024 - 2 * t - sizeof(float) * 2 * kTcCand * kTcEpiThreads) / t;
   return static_cast<int>(n < kTcMaxStages ? n : kTcMaxStages);
 }
 inline size_t search_tc_smem_bytes(int l) {
-  return 1024 + (2 + static_cast<size_t>(tc_stages(l))) * tc_tile_bytes(l) + sizeof(float) * 2 * kTcCand * kTcRows;
+  return 1024 + (2 + static_cast<size_t>(tc_stages(l))) * tc_tile_bytes(l) +
+         sizeof(float) * 2 * kTcCand * kTcEpiThreads;
 }
 // Upper bound of the search groups of the tensor-core plan (groups of <= 128 slots of one table).
 __host__ __device__ inline int64_t tc_max_groups(int64_t pairs, int ntab) {
@@ -193,15 +195,40 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
-      "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
         "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+// 64 consecutive columns of this warp's 32 lanes in one load, waited for inside the same
+// asm statement (the destination registers are defined only once the data has landed).
+__device__ __forceinline__ void tc_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -233,30 +260,41 @@ __device__ __forceinline__ float tc_exact(const float* q, const float* kp, int L
   return e;
 }
 
-// A full candidate list (n == kTcCand entries of slot r in s_cc/s_cv): drop the entries that
-// fell below amax - tw; if none did, rescore them all into s_mine[r] and empty the list.
-// Returns the new length. Kept out of line: the filter loop that calls it is unrolled, and
-// this path is rare.
-__device__ __noinline__ int tc_make_room(int r, float amax, float tw, const float* q, const float* kt,
-                                         int64_t sk, int L, uint32_t idx_offset, int* s_cc, float* s_cv,
-                                         unsigned long long* s_mine) {
+// A full candidate list (kTcCand entries of epilogue thread e in s_cc/s_cv, stride
+// kTcEpiThreads): drop the entries that fell below thr; if none did, rescore them all into
+// s_mine[e] and empty the list. Returns the new length. Kept out of line: the filter loop
+// that calls it is unrolled, and this path is rare.
+__device__ __noinline__ int tc_make_room(int e, float thr, const float* q, const float* kt, int64_t sk, int L,
+                                         uint32_t idx_offset, int* s_cc, float* s_cv, unsigned long long* s_mine) {
   int m = 0;
   for (int i = 0; i < kTcCand; ++i)
-    if (s_cv[i * kTcRows + r] >= amax - tw) {
-      s_cc[m * kTcRows + r] = s_cc[i * kTcRows + r];
-      s_cv[m * kTcRows + r] = s_cv[i * kTcRows + r];
+    if (s_cv[i * kTcEpiThreads + e] >= thr) {
+      s_cc[m * kTcEpiThreads + e] = s_cc[i * kTcEpiThreads + e];
+      s_cv[m * kTcEpiThreads + e] = s_cv[i * kTcEpiThreads + e];
       ++m;
     }
   if (m < kTcCand) return m;
-  unsigned long long mine = s_mine[r];
+  unsigned long long mine = s_mine[e];
   for (int i = 0; i < kTcCand; ++i) {
-    const int kr = s_cc[i * kTcRows + r];
+    const int kr = s_cc[i * kTcEpiThreads + e];
     const unsigned long long c = pack_cand(tc_exact(q, kt + static_cast<int64_t>(kr) * sk, L),
                                            idx_offset + static_cast<uint32_t>(kr));
     mine = c > mine ? c : mine;
   }
-  s_mine[r] = mine;
+  s_mine[e] = mine;
   return 0;
+}
+
+// Maximum of 32 values as a depth-5 tree (independent operations, no serial chain).
+__device__ __forceinline__ float tc_max32(const float (&v)[32]) {
+  float m[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) m[j] = fmaxf(v[j], v[j + 16]);
+#pragma unroll
+  for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+    for (int j = 0; j < w; ++j) m[j] = fmaxf(m[j], m[j + w]);
+  return m[0];
 }
 
 // ---- scan ------------------------------------------------------------------------------------
@@ -306,9 +344,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
   uint64_t* drain = t_empty + 2;                      // [1]
   unsigned char* sA = tsm + 1024;                     // [2][tile]
   unsigned char* sK = sA + 2 * tb;                    // [NS][tile]
-  int* s_cc = reinterpret_cast<int*>(sK + static_cast<size_t>(NS) * tb);  // [kTcCand][128]
-  float* s_cv = reinterpret_cast<float*>(s_cc + kTcCand * kTcRows);       // [kTcCand][128]
-  __shared__ unsigned long long s_mine[kTcRows];  // slot r's best exactly rescored candidate
+  int* s_cc = reinterpret_cast<int*>(sK + static_cast<size_t>(NS) * tb);  // [kTcCand][256]
+  float* s_cv = reinterpret_cast<float*>(s_cc + kTcCand * kTcEpiThreads);  // [kTcCand][256]
+  __shared__ unsigned long long s_mine[kTcEpiThreads];  // best exactly rescored candidate
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_issued, s_groups_issued;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -318,7 +356,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
   const int t_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * ntiles / gridDim.x);
   const int t_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * ntiles / gridDim.x);
   if (t_begin >= t_end) return;
-  if (warp == 5) {
+  if (warp == kTcMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
                  "r"(kTcTmemCols)
                  : "memory");
@@ -333,7 +371,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       mbar_init(&a_full[i], 1);
       mbar_init(&a_empty[i], 1);
       mbar_init(&t_full[i], 1);
-      mbar_init(&t_empty[i], kTcEpiThreads / 32);
+      mbar_init(&t_empty[i], kTcEpiThreads / 32);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -346,7 +384,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
-  if (warp == 4) {
+  if (warp == kTcProducerWarp) {
     // ---- producer --------------------------------------------------------------------------
     if (lane == 0) {
       int gi = -1, prev = -1, it = 0;
@@ -380,7 +418,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
         atomicOr(a.err, 8);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kTcMmaWarp) {
     // ---- MMA issuer ------------------------------------------------------------------------
     if (lane == 0) {
       int gi = -1, prev = -1, it = 0;
@@ -416,22 +454,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       }
     }
   } else {
-    // ---- epilogue: thread r = slot r of the group ---------------------------------------------
-    const int r = tid;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. (slots), columns 64 (w / 4) ..
+    // (centroids); thread e keeps the running maximum and candidates of its (slot, half).
+    const int e = tid;
+    const int r = (warp & 3) * 32 + lane;
+    const int half = warp >> 2;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     int prev = -1, p = -1, n = 0, it = 0;
     float amax = -INFINITY, tw = 0.f;
     const float* q = nullptr;
     const float* kt = nullptr;
     for (int tile = t_begin; tile < t_end; ++tile, ++it) {
-      const int g = tile / a.nchunks, c = tile % a.nchunks;
+      const int g = tile / a.nchunks, c = tile - g * a.nchunks;
       if (g != prev) {
         prev = g;
         const int4 gg = a.groups[g];
         const int table = gg.x;
         p = r < gg.z ? a.sorted[gg.y + r] : -1;
         n = 0;
-        s_mine[r] = 0ull;
+        s_mine[e] = 0ull;
         amax = -INFINITY;
         if (p >= 0) {
           const float delta = (0x1p-8f + 0x1p-11f) * a.qnorm[static_cast<int64_t>(g) * kTcRows + r] * a.knorm[table];
@@ -456,67 +497,71 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
         break;
       }
       tc_fence_after();
+      float v[64];
       {
         TC_T0();
-        const int rows = min(kTcRows, a.k - c * kTcRows);
-        const int kb = c * kTcRows;
-        for (int c0 = 0; c0 < kTcRows; c0 += 32) {
-          float v[32];
-          __syncwarp();
-          tc_ld32(lane_base + static_cast<uint32_t>(acc * kTcRows + c0), v);
-          if (p < 0) continue;
-          if (c0 + 32 > rows) {  // ragged last chunk
+        __syncwarp();
+        tc_ld64(lane_base + static_cast<uint32_t>(acc * kTcRows + half * 64), v);
+        TC_ACC(41);
+      }
+      // The accumulator may be overwritten as soon as every warp has its values.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&t_empty[acc]);
+      if (p >= 0) {
+        TC_T0();
+        const int rows = min(kTcRows, a.k - c * kTcRows) - half * 64;  // valid columns of this half
+        const int kb = c * kTcRows + half * 64;
+        if (rows < 64) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (c0 + j >= rows) v[j] = -INFINITY;
-          }
-          float m32 = v[0];
+          for (int j = 0; j < 64; ++j)
+            if (j >= rows) v[j] = -INFINITY;
+        }
+        const float m0 = tc_max32(*reinterpret_cast<const float(*)[32]>(v)),
+                    m1 = tc_max32(*reinterpret_cast<const float(*)[32]>(v + 32));
+        // Masked columns (-inf) never qualify, even while amax is still -inf.
+        if (fmaxf(m0, m1) > -INFINITY && fmaxf(m0, m1) >= amax - tw) {  // rare once amax has settled
+          amax = fmaxf(amax, fmaxf(m0, m1));
+          const float thr = amax - tw;
 #pragma unroll
-          for (int j = 1; j < 32; ++j) m32 = fmaxf(m32, v[j]);
-          if (!(m32 >= amax - tw)) continue;  // nothing in these 32 columns can be the best
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (v[j] >= amax - tw) {
-              amax = fmaxf(amax, v[j]);
-              if (n == kTcCand)
-                n = tc_make_room(r, amax, tw, q, kt, a.key_stride_k, L, a.idx_offset, s_cc, s_cv, s_mine);
-              s_cc[n * kTcRows + r] = kb + c0 + j;
-              s_cv[n * kTcRows + r] = v[j];
+          for (int j = 0; j < 64; ++j) {
+            const float x = v[j];
+            if (x >= thr && x > -INFINITY) {
+              if (n == kTcCand) n = tc_make_room(e, thr, q, kt, a.key_stride_k, L, a.idx_offset, s_cc, s_cv, s_mine);
+              s_cc[n * kTcEpiThreads + e] = kb + j;
+              s_cv[n * kTcEpiThreads + e] = x;
               ++n;
             }
           }
         }
-        TC_ACC(41);
-      }
-      // This accumulator may be overwritten now.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&t_empty[acc]);
-      if (p >= 0 && (tile + 1 == t_end || (tile + 1) / a.nchunks != g)) {
-        TC_T0();
-        unsigned long long mine = s_mine[r];
-        for (int i = 0; i < n; ++i) {
-          if (s_cv[i * kTcRows + r] < amax - tw) continue;
-          const int kr = s_cc[i * kTcRows + r];
-          const unsigned long long cand = pack_cand(tc_exact(q, kt + static_cast<int64_t>(kr) * a.key_stride_k, L),
-                                                    a.idx_offset + static_cast<uint32_t>(kr));
-          TC_COUNT();
-          mine = cand > mine ? cand : mine;
+        TC_ACC(43);
+        if (tile + 1 == t_end || (tile + 1) / a.nchunks != g) {
+          TC_T0();
+          unsigned long long mine = s_mine[e];
+          for (int i = 0; i < n; ++i) {
+            if (s_cv[i * kTcEpiThreads + e] < amax - tw) continue;
+            const int kr = s_cc[i * kTcEpiThreads + e];
+            const unsigned long long cand =
+                pack_cand(tc_exact(q, kt + static_cast<int64_t>(kr) * a.key_stride_k, L),
+                          a.idx_offset + static_cast<uint32_t>(kr));
+            TC_COUNT();
+            mine = cand > mine ? cand : mine;
+          }
+          n = 0;
+          if (mine) atomicMax(reinterpret_cast<unsigned long long*>(a.best + p), mine);
+          TC_ACC(42);
         }
-        n = 0;
-        if (mine) atomicMax(reinterpret_cast<unsigned long long*>(a.best + p), static_cast<unsigned long long>(mine));
-        TC_ACC(42);
       }
     }
   }
 
   __syncthreads();
-  if (*abort_flag && tid == 32 * 5) {
+  if (*abort_flag && tid == 32 * kTcMmaWarp) {
     // The MMAs this thread issued: a commit after them, waited (bounded).
     tc_commit(drain);
     mbar_wait_bounded(drain, 0);
   }
-  if (*abort_flag && tid == 32 * 4) {
+  if (*abort_flag && tid == 32 * kTcProducerWarp) {
     // Every copy this CTA issued: the latest use of each stage and query buffer (bounded).
     const int issued = s_issued, gissued = s_groups_issued;
     for (int st = 0; st < NS && st < issued; ++st) {
@@ -529,7 +574,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
     }
   }
   __syncthreads();
-  if (warp == 5)
+  if (warp == kTcMmaWarp)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
 }
 
