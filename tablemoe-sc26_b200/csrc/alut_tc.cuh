@@ -42,10 +42,11 @@ constexpr int kTcEpiThreads = 256;  // warps 0-7: (TMEM lane quarter, column hal
 constexpr int kTcThreads = 320;     // + producer warp 8 + MMA warp 9
 constexpr int kTcProducerWarp = 8, kTcMmaWarp = 9;
 constexpr int kTcMinPairs = 512;    // below this the CUDA-core scans are used
-constexpr int kTcCand = 4;          // candidate list per slot
+constexpr int kTcCand = 8;          // candidate list per (slot, column half)
 constexpr int kTcMaxStages = 8;
-constexpr uint32_t kTcTmemCols = 2 * kTcRows;  // two fp32 128x128 accumulators
-constexpr size_t kTcSmemBudget = 200 * 1024;
+constexpr int kTcAcc = 4;                          // fp32 128x128 accumulators in TMEM
+constexpr uint32_t kTcTmemCols = kTcAcc * kTcRows;  // all 512 columns: one CTA per SM
+constexpr size_t kTcSmemBudget = 212 * 1024;
 
 // Byte offset of element (row, k) in a [rows][L] bf16 operand in the K-major, no-swizzle
 // core-matrix order: 8-row x 16-byte core matrices, k-chunks adjacent (128 B apart), 8-row
@@ -246,18 +247,35 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
 }
 
 // Exact fp32 score of one centroid row: sequential fmaf over l (the CUDA-core scans' order).
+// L % 16 == 0: rows are read 32 values (8 float4 of each) at a time, all in flight before
+// the dependent FMAs.
 __device__ __forceinline__ float tc_exact(const float* q, const float* kp, int L) {
   float e = 0.f;
-#pragma unroll 4
-  for (int l = 0; l < L; l += 4) {
-    const float4 a = *reinterpret_cast<const float4*>(q + l);
-    const float4 b = __ldg(reinterpret_cast<const float4*>(kp + l));
-    e = fmaf(b.x, a.x, e);
-    e = fmaf(b.y, a.y, e);
-    e = fmaf(b.z, a.z, e);
-    e = fmaf(b.w, a.w, e);
+  for (int l0 = 0; l0 < L; l0 += 32) {
+    float4 a[8], b[8];
+    const int nv = min(8, (L - l0) / 4);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < nv) {
+        a[i] = *reinterpret_cast<const float4*>(q + l0 + 4 * i);
+        b[i] = __ldg(reinterpret_cast<const float4*>(kp + l0 + 4 * i));
+      }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < nv) {
+        e = fmaf(b[i].x, a[i].x, e);
+        e = fmaf(b[i].y, a[i].y, e);
+        e = fmaf(b[i].z, a[i].z, e);
+        e = fmaf(b[i].w, a[i].w, e);
+      }
   }
   return e;
+}
+
+// Packed exact candidate of centroid row kr (out of line: rare, and register-hungry).
+__device__ __noinline__ unsigned long long tc_rescore(const float* q, const float* kt, int64_t sk, int L, int kr,
+                                                      uint32_t idx_offset) {
+  return pack_cand(tc_exact(q, kt + static_cast<int64_t>(kr) * sk, L), idx_offset + static_cast<uint32_t>(kr));
 }
 
 // A full candidate list (kTcCand entries of epilogue thread e in s_cc/s_cv, stride
@@ -276,9 +294,7 @@ __device__ __noinline__ int tc_make_room(int e, float thr, const float* q, const
   if (m < kTcCand) return m;
   unsigned long long mine = s_mine[e];
   for (int i = 0; i < kTcCand; ++i) {
-    const int kr = s_cc[i * kTcEpiThreads + e];
-    const unsigned long long c = pack_cand(tc_exact(q, kt + static_cast<int64_t>(kr) * sk, L),
-                                           idx_offset + static_cast<uint32_t>(kr));
+    const unsigned long long c = tc_rescore(q, kt, sk, L, s_cc[i * kTcEpiThreads + e], idx_offset);
     mine = c > mine ? c : mine;
   }
   s_mine[e] = mine;
@@ -324,10 +340,18 @@ struct TcArgs {
   if (blockIdx.x == 0 && threadIdx.x == 0) g_alut_trace[slot] += global_ns() - tc_t0_
 #define TC_COUNT() \
   if (blockIdx.x == 0) atomicAdd(&g_alut_trace[48], 1ull)
+#define TC_T0_TID(t) const uint64_t tc_t0_ = (blockIdx.x == 0 && threadIdx.x == (t)) ? global_ns() : 0
+#define TC_ACC_TID(t, slot) \
+  if (blockIdx.x == 0 && threadIdx.x == (t)) g_alut_trace[slot] += global_ns() - tc_t0_
+#define TC_INC_TID(t, slot) \
+  if (blockIdx.x == 0 && threadIdx.x == (t)) g_alut_trace[slot] += 1
 #else
 #define TC_T0() do {} while (0)
 #define TC_ACC(slot) do {} while (0)
 #define TC_COUNT() do {} while (0)
+#define TC_T0_TID(t) do {} while (0)
+#define TC_ACC_TID(t, slot) do {} while (0)
+#define TC_INC_TID(t, slot) do {} while (0)
 #endif
 
 __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
@@ -339,9 +363,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
   uint64_t* empty = full + kTcMaxStages;              // [kTcMaxStages]
   uint64_t* a_full = empty + kTcMaxStages;            // [2] query tiles
   uint64_t* a_empty = a_full + 2;                     // [2]
-  uint64_t* t_full = a_empty + 2;                     // [2] accumulators
-  uint64_t* t_empty = t_full + 2;                     // [2]
-  uint64_t* drain = t_empty + 2;                      // [1]
+  uint64_t* t_full = a_empty + 2;                     // [kTcAcc] accumulators
+  uint64_t* t_empty = t_full + kTcAcc;                // [kTcAcc]
+  uint64_t* drain = t_empty + kTcAcc;                 // [1]
   unsigned char* sA = tsm + 1024;                     // [2][tile]
   unsigned char* sK = sA + 2 * tb;                    // [NS][tile]
   int* s_cc = reinterpret_cast<int*>(sK + static_cast<size_t>(NS) * tb);  // [kTcCand][256]
@@ -370,6 +394,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&a_full[i], 1);
       mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < kTcAcc; ++i) {
       mbar_init(&t_full[i], 1);
       mbar_init(&t_empty[i], kTcEpiThreads / 32);  // one arrival per epilogue warp
     }
@@ -403,7 +429,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
           bulk_g2s(sA + ab * tb, a.qsplit + static_cast<int64_t>(g) * tb, tb, &a_full[ab]);
         }
         const int st = it % NS;
-        if (it >= NS && !tc_wait(&empty[st], ((it / NS) - 1) & 1, abort_flag)) {
+        bool w;
+        {
+          TC_T0_TID(32 * kTcProducerWarp);
+          w = it < NS || tc_wait(&empty[st], ((it / NS) - 1) & 1, abort_flag);
+          TC_ACC_TID(32 * kTcProducerWarp, 52);
+        }
+        if (!w) {
           ok = false;
           break;
         }
@@ -433,9 +465,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
             break;
           }
         }
-        const int st = it % NS, acc = it & 1;
-        if (!tc_wait(&full[st], (it / NS) & 1, abort_flag) ||
-            (it >= 2 && !tc_wait(&t_empty[acc], ((it >> 1) - 1) & 1, abort_flag))) {
+        const int st = it % NS, acc = it % kTcAcc;
+        bool w1, w2;
+        {
+          TC_T0_TID(32 * kTcMmaWarp);
+          w1 = tc_wait(&full[st], (it / NS) & 1, abort_flag);
+          TC_ACC_TID(32 * kTcMmaWarp, 50);
+        }
+        {
+          TC_T0_TID(32 * kTcMmaWarp);
+          w2 = w1 && (it < kTcAcc || tc_wait(&t_empty[acc], ((it / kTcAcc) - 1) & 1, abort_flag));
+          TC_ACC_TID(32 * kTcMmaWarp, 51);
+        }
+        if (!w1 || !w2) {
           ok = false;
           break;
         }
@@ -482,11 +524,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
                static_cast<int64_t>(table & 1) * a.key_stride_m;
         }
       }
-      const int acc = it & 1;
+      const int acc = it % kTcAcc;
       bool ok;
       {
         TC_T0();
-        ok = tc_wait(&t_full[acc], (it >> 1) & 1, abort_flag);
+        ok = tc_wait(&t_full[acc], (it / kTcAcc) & 1, abort_flag);
         TC_ACC(40);
       }
       if (__any_sync(0xffffffffu, !ok)) {
@@ -508,7 +550,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&t_empty[acc]);
+#ifdef ALUT_TC_EXPERIMENT_NO_FILTER
+      if (v[0] == 12345.f) atomicAdd(a.err, 0);  // keeps the load live
+      if (false) {
+#else
       if (p >= 0) {
+#endif
         TC_T0();
         const int rows = min(kTcRows, a.k - c * kTcRows) - half * 64;  // valid columns of this half
         const int kb = c * kTcRows + half * 64;
@@ -521,17 +568,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
                     m1 = tc_max32(*reinterpret_cast<const float(*)[32]>(v + 32));
         // Masked columns (-inf) never qualify, even while amax is still -inf.
         if (fmaxf(m0, m1) > -INFINITY && fmaxf(m0, m1) >= amax - tw) {  // rare once amax has settled
+          TC_INC_TID(0, 45);
           amax = fmaxf(amax, fmaxf(m0, m1));
           const float thr = amax - tw;
+          // Qualifying columns as bit masks (predicated compares, no branches), then one
+          // insertion per set bit - usually one.
+          uint32_t mk0 = 0u, mk1 = 0u;
 #pragma unroll
-          for (int j = 0; j < 64; ++j) {
-            const float x = v[j];
-            if (x >= thr && x > -INFINITY) {
-              if (n == kTcCand) n = tc_make_room(e, thr, q, kt, a.key_stride_k, L, a.idx_offset, s_cc, s_cv, s_mine);
-              s_cc[n * kTcEpiThreads + e] = kb + j;
-              s_cv[n * kTcEpiThreads + e] = x;
-              ++n;
+          for (int j = 0; j < 32; ++j) {
+            mk0 |= (v[j] >= thr ? 1u : 0u) << j;
+            mk1 |= (v[32 + j] >= thr ? 1u : 0u) << j;
+          }
+          const uint64_t mk = (static_cast<uint64_t>(mk1) << 32) | mk0;
+          // The stored value: with one qualifying column it is the slice maximum itself; with
+          // several, amax - an upper bound, so pruning never drops a column that could win.
+          const float x = __popcll(static_cast<long long>(mk)) == 1 ? fmaxf(m0, m1) : amax;
+          for (uint64_t m = mk; m; m &= m - 1) {
+            const int j = __ffsll(static_cast<long long>(m)) - 1;
+            if (n == kTcCand) {
+              TC_INC_TID(0, 46);
+              n = tc_make_room(e, thr, q, kt, a.key_stride_k, L, a.idx_offset, s_cc, s_cv, s_mine);
             }
+            s_cc[n * kTcEpiThreads + e] = kb + j;
+            s_cv[n * kTcEpiThreads + e] = x;
+            ++n;
           }
         }
         TC_ACC(43);
@@ -540,10 +600,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
           unsigned long long mine = s_mine[e];
           for (int i = 0; i < n; ++i) {
             if (s_cv[i * kTcEpiThreads + e] < amax - tw) continue;
-            const int kr = s_cc[i * kTcEpiThreads + e];
             const unsigned long long cand =
-                pack_cand(tc_exact(q, kt + static_cast<int64_t>(kr) * a.key_stride_k, L),
-                          a.idx_offset + static_cast<uint32_t>(kr));
+                tc_rescore(q, kt, a.key_stride_k, L, s_cc[i * kTcEpiThreads + e], a.idx_offset);
             TC_COUNT();
             mine = cand > mine ? cand : mine;
           }
