@@ -550,12 +550,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&t_empty[acc]);
-#ifdef ALUT_TC_EXPERIMENT_NO_FILTER
-      if (v[0] == 12345.f) atomicAdd(a.err, 0);  // keeps the load live
-      if (false) {
-#else
       if (p >= 0) {
-#endif
         TC_T0();
         const int rows = min(kTcRows, a.k - c * kTcRows) - half * 64;  // valid columns of this half
         const int kb = c * kTcRows + half * 64;
