@@ -66,6 +66,21 @@ class ShardedCentroidTable:
             self._split = _alut.prepare_basis(self._tables, self.device)
             if self._split is not None:
                 self._tables.proj_split = self._split.data_ptr()
+            # bf16 operand form of this rank's keys for the tensor-core scan (fp32 keys,
+            # L % 16 == 0, L <= 128; other shapes keep the CUDA-core scans).
+            self._keys_split = None
+            if self.device.type == "cuda":
+                lib = _alut.load()
+                n = int(lib.alut_keys_split_bytes(self._tables))
+                if n:
+                    self._keys_split = torch.empty(n, dtype=torch.uint8, device=self.device)
+                    _alut.check(lib.alut_prepare_keys(self._tables, int(self.params["keyset"]),
+                                                      self._keys_split.data_ptr(), n, _alut.stream_ptr(self.device)),
+                                "alut_prepare_keys")
+                    if self.params["keyset"] == _alut.KEYS_RAW:
+                        self._tables.raw_keys_split = self._keys_split.data_ptr()
+                    else:
+                        self._tables.keys_split = self._keys_split.data_ptr()
         return self._tables
 
     def _params_struct(self):
