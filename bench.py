@@ -413,6 +413,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--wl-steps", type=int, default=20, help="timed steps of each secondary workload")
     ap.add_argument("--no-workloads", action="store_true", help="skip the config 3 / config 5 measurements")
+    ap.add_argument("--only", choices=["c3", "c5"], default=None,
+                    help="run only that secondary workload and print its JSON (profiling captures)")
     ap.add_argument("--layers", type=int, default=CFG["layers"],
                     help="fewer layers for profiling captures only (the benchmark is 48)")
     args = ap.parse_args()
@@ -429,6 +431,13 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world, device)
+        elif args.only:
+            peaks, _ = measured_peaks()
+            flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+            res = (c3_workload(args, device, flush, peaks) if args.only == "c3"
+                   else c5_workload(args, rank, world, device, flush, peaks))
+            if rank == 0:
+                print(json.dumps({"workload": args.only, **res}), flush=True)
         else:
             run_alut(args, rank, world, local, device)
     finally:

@@ -239,6 +239,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 
 // Bounded wait that also gives up when another role of the CTA has aborted.
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;  // the common case: no timer read
   const uint64_t t0 = global_ns();
   for (uint32_t n = 0;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -413,11 +414,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
   if (warp == kTcProducerWarp) {
     // ---- producer --------------------------------------------------------------------------
     if (lane == 0) {
-      int gi = -1, prev = -1, it = 0;
+      int gi = -1, prev = -1, it = 0, table = 0;
       bool ok = true;
       for (int tile = t_begin; tile < t_end && ok; ++tile, ++it) {
         const int g = tile / a.nchunks, c = tile % a.nchunks;
         if (g != prev) {
+          table = a.groups[g].x;
           const int ab = (gi + 1) & 1;
           if (gi + 1 >= 2 && !tc_wait(&a_empty[ab], (((gi + 1) >> 1) - 1) & 1, abort_flag)) {
             ok = false;
@@ -439,7 +441,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
           ok = false;
           break;
         }
-        const int table = a.groups[g].x;
         mbar_expect_tx(&full[st], tb);
         bulk_g2s(sK + st * tb, a.ksplit + (static_cast<int64_t>(table) * a.nchunks + c) * tb, tb, &full[st]);
       }
