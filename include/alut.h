@@ -97,9 +97,11 @@ typedef struct alut_tables {
   int64_t key_stride[3];   /* strides of dims e, m, k (keys and raw_keys share them) */
   int64_t value_stride[3]; /* strides of dims e, m, k */
   int64_t proj_stride_h;   /* row stride of proj */
-  /* Optional: the fp32 basis split into three bf16 parts, [2 modalities][3][L][H]
-   * (hi + mid + lo == proj to fp32 precision), written by alut_prepare_basis. When set and
-   * x is bf16, small batches project on tensor cores; NULL keeps the CUDA-core path. */
+  /* Optional: the fp32 basis split into three bf16 parts (hi + mid + lo == proj to fp32
+   * precision), written by alut_prepare_basis: [2 modalities][3][L][H], followed (when
+   * L % 16 == 0, L <= 128 and H % 64 == 0) by the same parts in the large-batch tensor-core
+   * projection's operand order. When set and x is bf16, the projection runs on tensor
+   * cores; NULL keeps the CUDA-core path. */
   const void* proj_split;
   /* Optional: fp32 key tables prepared for the tensor-core scan by alut_prepare_keys
    * (keys_split for keys, raw_keys_split for raw_keys; NULL keeps the CUDA-core scans). */
@@ -139,7 +141,7 @@ typedef struct alut_search_params {
 size_t alut_workspace_size(const alut_tables_t* tables, int32_t q, int32_t s);
 
 /* Bytes of the split basis of these tables (0 if the tables do not qualify: fp32 proj,
- * H % 16 == 0, L % 8 == 0). */
+ * H % 16 == 0, L % 8 == 0); includes the operand-order copy when the shape allows it. */
 size_t alut_basis_split_bytes(const alut_tables_t* tables);
 
 /* Write the split basis (see alut_tables_t.proj_split) of tables->proj into out, a device
@@ -148,8 +150,11 @@ int alut_prepare_basis(const alut_tables_t* tables, void* out, size_t out_bytes,
 
 /* Bytes of the tensor-core form of one fp32 key set of these tables (0 if they do not
  * qualify: fp32 keys, L % 16 == 0, L <= 128): every (expert, modality) table cut into
- * 128-row chunks, each chunk as two bf16 parts (hi, lo = keys - hi) in the tensor cores'
- * K-major core-matrix order, followed by the largest row norm of every table. */
+ * 128-row chunks, each chunk as bf16 (round to nearest) in the tensor cores' K-major
+ * core-matrix order, followed by the largest row norm of every table. The tensor-core
+ * scan uses it only to choose candidates; every candidate is rescored in fp32 from the
+ * original keys, so results equal the CUDA-core scans'. Used for batches of >= 512
+ * searched slots when the workspace has room (alut_workspace_size includes it). */
 size_t alut_keys_split_bytes(const alut_tables_t* tables);
 
 /* Write that form of the key set `keyset` into out (device, alut_keys_split_bytes bytes).
