@@ -223,6 +223,29 @@ int alut_merge_packed(int32_t world, int32_t q, int32_t s, const uint64_t* packe
                       const uint8_t* is_vision, const alut_search_params_t* params,
                       uint8_t* out_hit, int64_t* out_idx, alut_stream_t stream);
 
+/* ---- peer access for the centroid-range shards (new; no reference counterpart) ----------
+ * Each rank exports the device allocation holding its value slice as a CUDA IPC handle
+ * (ALUT_PEER_HANDLE_BYTES bytes, plus the slice's offset inside the allocation), the
+ * ranks exchange them over their process group, and each opens its peers' handles (peer
+ * access over NVLink, no multicast). alut_peer_close undoes alut_peer_open. */
+#define ALUT_PEER_HANDLE_BYTES 64
+int alut_peer_export(const void* ptr, void* handle, uint64_t* offset);
+int alut_peer_open(const void* handle, uint64_t offset, void** ptr);
+int alut_peer_close(void* ptr, uint64_t offset);
+
+/* out[i] (row stride out_stride elements) = the value row of centroid idx[i] (global index)
+ * and modality (is_vision[i] ? 0 : 1), read from the shard that owns it; zeros where
+ * hit[i] == 0. shard_values, shard_start and shard_stride_m are DEVICE arrays: world
+ * pointers to each shard's [2][Kr][H] value slice (the caller's own and its peers'
+ * alut_peer_open mappings), world + 1 centroid boundaries, and each slice's modality
+ * stride in elements; every slice has row stride value_stride_k. Rows are h elements of
+ * value_dtype, a whole number of 16-byte units. Replaces the gather + reduce-scatter row
+ * exchange of the sharded lookup: each remote row crosses NVLink once. */
+int alut_gather_rows_sharded(int32_t n, const uint8_t* hit, const int64_t* idx, const uint8_t* is_vision,
+                             int32_t world, const void* const* shard_values, const int64_t* shard_start,
+                             const int64_t* shard_stride_m, int64_t value_stride_k, int32_t h, int32_t value_dtype,
+                             void* out, int64_t out_stride, alut_stream_t stream);
+
 /* alut_lookup_combine for callers that cannot allocate device memory: those handed only
  * their input and output buffers by another runtime (an FFI host without access to the
  * CUDA allocator, a serving loop that forbids cudaMalloc after start-up because it can

@@ -7,12 +7,15 @@
 #include <algorithm>
 #include <mutex>
 
+#include <cuda.h>
+
 #include "alut_combine.cuh"
 #include "alut_common.cuh"
 #include "alut_project.cuh"
 #include "alut_search.cuh"
 #include "alut_tc.cuh"
 #include "alut_project_tc.cuh"
+#include "alut_peer.cuh"
 
 namespace alut {
 
@@ -602,6 +605,76 @@ int alut_debug_trace(unsigned long long* host, int n) {
   return cudaMemcpyFromSymbol(host, g_alut_trace, sizeof(unsigned long long) * (n < 64 ? n : 64)) == cudaSuccess ? 0 : -4;
 }
 #endif
+
+// ---- peer access for the centroid-range shards (CUDA IPC; no multicast objects) -------------
+
+static_assert(sizeof(cudaIpcMemHandle_t) <= ALUT_PEER_HANDLE_BYTES, "IPC handle size");
+
+int alut_peer_export(const void* ptr, void* handle, uint64_t* offset) {
+  if (!ptr || !handle || !offset) return fail(ALUT_EINVAL, "peer_export: NULL argument");
+  // The handle names the whole allocation; the offset locates ptr inside it.
+  using GetRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static GetRange get_range = nullptr;
+  if (!get_range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return fail(ALUT_ECUDA, "peer_export: cuMemGetAddressRange unavailable");
+    get_range = reinterpret_cast<GetRange>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (get_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(ALUT_ECUDA, "peer_export: pointer is not device memory");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "peer_export: %s", cudaGetErrorString(e));
+  memset(handle, 0, ALUT_PEER_HANDLE_BYTES);
+  memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<uint64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return ALUT_OK;
+}
+
+int alut_peer_open(const void* handle, uint64_t offset, void** ptr) {
+  if (!handle || !ptr) return fail(ALUT_EINVAL, "peer_open: NULL argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "peer_open: %s", cudaGetErrorString(e));
+  *ptr = static_cast<char*>(base) + offset;
+  return ALUT_OK;
+}
+
+int alut_peer_close(void* ptr, uint64_t offset) {
+  if (!ptr) return ALUT_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset);
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "peer_close: %s", cudaGetErrorString(e));
+  return ALUT_OK;
+}
+
+int alut_gather_rows_sharded(int32_t n, const uint8_t* hit, const int64_t* idx, const uint8_t* is_vision,
+                             int32_t world, const void* const* shard_values, const int64_t* shard_start,
+                             const int64_t* shard_stride_m, int64_t value_stride_k, int32_t h, int32_t value_dtype,
+                             void* out, int64_t out_stride, alut_stream_t stream) {
+  if (n < 0 || world < 1 || world > kPeerMaxWorld) return fail(ALUT_EINVAL, "gather_rows_sharded: n=%d world=%d", n, world);
+  if (n == 0) return ALUT_OK;
+  if (!hit || !idx || !is_vision || !shard_values || !shard_start || !shard_stride_m || !out)
+    return fail(ALUT_EINVAL, "gather_rows_sharded: NULL argument");
+  if (!dtype_ok(value_dtype)) return fail(ALUT_EDTYPE, "gather_rows_sharded: value dtype");
+  const int esz = dtype_size(value_dtype);
+  const int64_t row_bytes = static_cast<int64_t>(h) * esz;
+  if (h <= 0 || row_bytes % 16 != 0 || value_stride_k < h || out_stride < h ||
+      (value_stride_k * esz) % 16 != 0 || (out_stride * esz) % 16 != 0 || !aligned16(out))
+    return fail(ALUT_ESHAPE, "gather_rows_sharded: rows must be whole 16-byte units (h=%d)", h);
+  const int grid = ceil_div(n, kPeerThreads / 32);
+  k_gather_sharded<<<grid, kPeerThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      n, hit, idx, is_vision, world, reinterpret_cast<const unsigned char* const*>(shard_values), shard_start,
+      shard_stride_m, esz, value_stride_k * esz, static_cast<int>(row_bytes), static_cast<unsigned char*>(out),
+      out_stride * esz);
+  return check_launch("k_gather_sharded");
+}
 
 int alut_set_profile_events(void* start_event, void* stop_event) {
   if ((start_event == nullptr) != (stop_event == nullptr))

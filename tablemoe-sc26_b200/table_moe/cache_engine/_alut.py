@@ -23,6 +23,7 @@ ALUT_EINVAL, ALUT_EDTYPE, ALUT_ESHAPE, ALUT_ECUDA, ALUT_EWORKSPACE, ALUT_ERANGE 
 KEYS_NORMALISED, KEYS_RAW = 0, 1
 RENORM_NONE, RENORM_TO_ONE, RENORM_TO_ROWSUM = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 2 << 20  # ALUT_NOALLOC_SCRATCH_BYTES
+PEER_HANDLE_BYTES = 64  # ALUT_PEER_HANDLE_BYTES
 
 _DTYPE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
@@ -82,6 +83,11 @@ SIGNATURES = {
                                                    _I32, _P, _P, _I64, _P]),
     "alut_search_packed": (ctypes.c_int, [_TP, _BP, _PP, _P, _I64, _P, _P, _SZ, _P]),
     "alut_merge_packed": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _PP, _P, _P, _P]),
+    "alut_peer_export": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_uint64)]),
+    "alut_peer_open": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]),
+    "alut_peer_close": (ctypes.c_int, [_P, ctypes.c_uint64]),
+    "alut_gather_rows_sharded": (ctypes.c_int, [_I32, _P, _P, _P, _I32, _P, _P, _P, _I64, _I32, _I32, _P, _I64,
+                                                _P]),
     "alut_set_profile_events": (ctypes.c_int, [_P, _P]),
     "alut_last_error": (ctypes.c_char_p, []),
     "alut_version": (ctypes.c_int, []),

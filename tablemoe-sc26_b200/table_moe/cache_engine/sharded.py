@@ -3,15 +3,20 @@
 Rank r of W holds centroids [K*r/W, K*(r+1)/W) of the key table and the matching value
 rows. A lookup of Q tokens then runs in three steps:
 
-1. every rank scans its slice for all Q tokens (``alut_search_packed``), producing one
-   packed candidate per token: ``(order-preserving score bits << 32) | (0xFFFFFFFF - global
-   index)``, so that the largest packed value is the best score with the lowest index;
+1. every rank projects its slice of Q/W tokens and the projected queries are exchanged
+   (``all_gather_into_tensor``, Q x L fp32), then every rank scans its centroid slice for
+   all Q tokens (``alut_search_packed``), producing one packed candidate per token:
+   ``(order-preserving score bits << 32) | (0xFFFFFFFF - global index)``, so that the
+   largest packed value is the best score with the lowest index;
 2. the W candidate vectors are exchanged (``all_gather_into_tensor``, 8 bytes per token per
    rank) and merged by max (``alut_merge_packed``), which also applies the hit rule - every
    rank now holds the winners;
-3. each rank gathers the winning rows it owns (rows owned elsewhere, and misses, come out
-   as zeros) and a ``reduce_scatter_tensor`` (sum) hands each rank its slice of Q/W tokens;
-   a row has one non-zero contribution, so the sum is an exact copy.
+3. each rank reads the rows of its own Q/W tokens straight from the owning rank's HBM
+   (``alut_gather_rows_sharded`` over CUDA IPC peer mappings, NVLink loads, no multicast):
+   every remote row crosses NVLink once. Groups that cannot map peer memory (gloo, or
+   IPC unavailable) use the collective form instead: each rank gathers the rows it owns
+   (zeros elsewhere) and a reduce-scatter (sum) hands out the token slices - a row has
+   one non-zero contribution, so the sum is an exact copy.
 
 The reference is single-GPU; this is the centroid-range sharding the benchmark's large-
 table configuration asks for. The device work goes through the C ABI; the three device
@@ -51,6 +56,7 @@ class ShardedCentroidTable:
                            thr_text=thr_text, eps=eps)
         self._tables = None
         self._ws = None
+        self._peers = None  # (device pointers, shard starts, modality strides, opened mappings)
         # Device steps (replaceable for CPU tests of the exchange).
         self.local_search = self._local_search
         self.merge = self._merge
@@ -130,10 +136,115 @@ class ShardedCentroidTable:
         _alut.check(rc, "alut_gather_rows")
         return out
 
+    def _nccl(self):
+        return self.world > 1 and self.device.type == "cuda" and dist.get_backend(self.group) == "nccl"
+
+    def _project_split(self, x, is_vision):
+        """This rank projects its Q/W tokens; the ranks all-gather the queries -> [Q, L] fp32."""
+        lib = _alut.load()
+        q = x.shape[0]
+        lo, hi = q * self.rank // self.world, q * (self.rank + 1) // self.world
+        t = self._tables_struct()
+        need = int(lib.alut_workspace_size(t, q, 1))
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        xs = x[lo:hi]
+        vs = is_vision.reshape(-1)[lo:hi].bool().contiguous()
+        sel = torch.zeros(hi - lo, 1, dtype=torch.int64, device=self.device)
+        mine = torch.empty(hi - lo, t.l, dtype=torch.float32, device=self.device)
+        b = _alut.make_batch(xs, sel, vs, None)  # xs, sel, vs stay referenced until the call returns
+        _alut.check(lib.alut_project(t, ctypes.byref(b), int(self.params["normalize"]), self.params["eps"],
+                                     mine.data_ptr(), t.l, self._ws.data_ptr(), self._ws.numel(),
+                                     _alut.stream_ptr(self.device)), "alut_project")
+        q_all = torch.empty(q, t.l, dtype=torch.float32, device=self.device)
+        dist.all_gather_into_tensor(q_all, mine, group=self.group)
+        return q_all
+
+    def _local_search_q(self, q_all, is_vision):
+        """Packed best candidates of this slice for precomputed queries (normalisation, if
+        any, was applied by the projection)."""
+        lib = _alut.load()
+        q = q_all.shape[0]
+        t = self._tables_struct()
+        need = int(lib.alut_workspace_size(t, q, 1))
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        sel = torch.zeros(q, 1, dtype=torch.int64, device=self.device)
+        vis = is_vision.reshape(-1).bool().contiguous()
+        packed = torch.empty(q, dtype=torch.int64, device=self.device)
+        b = _alut.make_batch(None, sel, vis, None)
+        p = self.params
+        prm = _alut.make_params(p["keyset"], False, p["cmp_ge"], p["thr_vision"], p["thr_text"], p["eps"])
+        rc = lib.alut_search_packed(t, ctypes.byref(b), prm, q_all.data_ptr(), self.k0, packed.data_ptr(),
+                                    self._ws.data_ptr(), self._ws.numel(), _alut.stream_ptr(self.device))
+        _alut.check(rc, "alut_search_packed")
+        return packed
+
+    def _peer_setup(self):
+        """Exchange CUDA IPC handles of the value slices; False if peer mapping is unavailable."""
+        if self._peers is not None:
+            return self._peers is not False
+        lib = _alut.load()
+        v = self.values
+        ok = v.is_contiguous() and v.shape[0] == 1
+        handle = (ctypes.c_ubyte * _alut.PEER_HANDLE_BYTES)()
+        off = ctypes.c_uint64(0)
+        if ok:
+            ok = lib.alut_peer_export(v.data_ptr(), handle, ctypes.byref(off)) == 0
+        info = (bytes(handle), int(off.value), self.k0, self.k1, int(v.stride(1)), int(v.stride(2)), bool(ok))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, info, group=self.group)
+        if not all(e[6] for e in everyone) or len({e[5] for e in everyone}) != 1:
+            self._peers = False
+            return False
+        ptrs, opened = [], []
+        for r, (h, o, _k0, _k1, _sm, _sk, _ok) in enumerate(everyone):
+            if r == self.rank:
+                ptrs.append(v.data_ptr())
+                continue
+            p = ctypes.c_void_p()
+            _alut.check(lib.alut_peer_open(h, o, ctypes.byref(p)), "alut_peer_open")
+            opened.append((p.value, o))
+            ptrs.append(p.value)
+        dev = self.device
+        self._peers = (torch.tensor(ptrs, dtype=torch.int64, device=dev),
+                       torch.tensor([e[2] for e in everyone] + [everyone[-1][3]], dtype=torch.int64, device=dev),
+                       torch.tensor([e[4] for e in everyone], dtype=torch.int64, device=dev), opened,
+                       everyone[0][5])
+        return True
+
+    def close(self):
+        """Unmap the peers' value slices (collective: every rank calls it before freeing its
+        values, so that no peer still reads them)."""
+        if self._peers:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            lib = _alut.load()
+            for p, o in self._peers[3]:
+                lib.alut_peer_close(p, o)
+        self._peers = None
+
+    def _gather_peer(self, hit, idx, is_vision, lo, hi):
+        lib = _alut.load()
+        ptrs, starts, strides_m, _opened, stride_k = self._peers
+        n = hi - lo
+        h = self.values.shape[-1]
+        out = torch.empty(n, h, dtype=self.values.dtype, device=self.device)
+        vis = is_vision.reshape(-1)[lo:hi].bool().contiguous()
+        rc = lib.alut_gather_rows_sharded(n, hit[lo:hi].contiguous().data_ptr(), idx[lo:hi].contiguous().data_ptr(),
+                                          vis.data_ptr(), self.world, ptrs.data_ptr(), starts.data_ptr(),
+                                          strides_m.data_ptr(), stride_k, h, _alut.dtype_code(self.values.dtype),
+                                          out.data_ptr(), out.stride(0), _alut.stream_ptr(self.device))
+        _alut.check(rc, "alut_gather_rows_sharded")
+        return out
+
     # ---- lookup ---------------------------------------------------------------------------
     def search(self, x, is_vision):
         """Global (hit, idx) of every token, identical on all ranks."""
-        packed = self.local_search(x, is_vision)
+        if self._nccl() and x.shape[0] % self.world == 0 and self.local_search == self._local_search:
+            packed = self._local_search_q(self._project_split(x, is_vision), is_vision)
+        else:
+            packed = self.local_search(x, is_vision)
         if self.world == 1:
             return self.merge(packed.view(1, -1), is_vision)
         flat = torch.empty(self.world * packed.numel(), dtype=packed.dtype, device=packed.device)
@@ -143,13 +254,16 @@ class ShardedCentroidTable:
     def lookup(self, x, is_vision):
         """Search, then the value rows of this rank's token slice [Q*r/W, Q*(r+1)/W) (Q must
         be a multiple of W): (hit [Q], idx [Q], rows [Q/W, H])."""
+        q = x.shape[0]
+        if self.world > 1 and q % self.world:
+            raise ValueError(f"token count {q} is not a multiple of the world size {self.world}")
         hit, idx = self.search(x, is_vision)
+        if self._nccl() and self.gather_owned == self._gather_owned and self._peer_setup():
+            lo, hi = q * self.rank // self.world, q * (self.rank + 1) // self.world
+            return hit, idx, self._gather_peer(hit, idx, is_vision, lo, hi)
         rows = self.gather_owned(hit, idx, is_vision)
         if self.world == 1:
             return hit, idx, rows
-        q = rows.shape[0]
-        if q % self.world:
-            raise ValueError(f"token count {q} is not a multiple of the world size {self.world}")
         n = q // self.world
         if dist.get_backend(self.group) == "gloo":  # CPU groups: no reduce_scatter in gloo
             rows = rows.contiguous().clone()
