@@ -280,11 +280,13 @@ static int launch_project(int key_dtype, int x_dtype, const ProjPlanArgs& a, cud
     p.q_out = static_cast<float*>(a.q_out);
     p.q_out_stride = a.q_out_stride;
     p.err = a.meta + 1;
+    CUtensorMap x_map;
+    if (!pt_encode_x_map(&x_map, a.x, a.q, a.h, a.x_stride)) return fail(ALUT_ECUDA, "project: tensor map of x");
     const size_t sm = pt_smem_bytes(a.l);
     int rc = allow_smem(reinterpret_cast<const void*>(k_project_tc), sm);
     if (rc) return rc;
     const int ntiles = ceil_div(a.q, kTcRows);
-    k_project_tc<<<std::min(ntiles, num_sms()), kPtThreads, sm, st>>>(p);
+    k_project_tc<<<std::min(ntiles, num_sms()), kPtThreads, sm, st>>>(x_map, p);
     return check_launch("k_project_tc");
   }
   if (mma_projection_ok(key_dtype, x_dtype, a)) {
@@ -488,6 +490,9 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     if (g_prof_start && g_prof_stop && record_profile(g_prof_stop, st)) return ALUT_ECUDA;
     return ALUT_OK;
   }
+  // Large batches: precomputed fp32 queries are read in place (no copy into the workspace).
+  const bool q_direct = q_low_in != nullptr && t->key_dtype == ALUT_F32 && aligned16(q_low_in);
+  if (q_direct) a.qlow = const_cast<float*>(static_cast<const float*>(q_low_in));
   // Large batches on fp32 tables prepared for it, with room in the workspace for the staged
   // queries: tensor-core scan (tcgen05).
   const void* ksplit = keys == t->raw_keys ? t->raw_keys_split : t->keys_split;
@@ -496,7 +501,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     a.group = kTcRows;
     int rc = launch_plan(a, reinterpret_cast<int*>(base + w.tabs), st);
     if (rc) return rc;
-    rc = launch_project(t->key_dtype, b->x_dtype, a, st);
+    if (!q_direct) rc = launch_project(t->key_dtype, b->x_dtype, a, st);
     if (rc) return rc;
     const int ntab = 2 * t->num_experts;
     const int nchunks = ceil_div(t->k, kTcRows);
@@ -543,7 +548,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
   }
   int rc = launch_plan(a, reinterpret_cast<int*>(base + w.tabs), st);
   if (rc) return rc;
-  rc = launch_project(t->key_dtype, b->x_dtype, a, st);
+  if (!q_direct) rc = launch_project(t->key_dtype, b->x_dtype, a, st);
   if (rc) return rc;
 
   SearchArgs s{};

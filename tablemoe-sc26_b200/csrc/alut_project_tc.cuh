@@ -6,19 +6,20 @@
 // `_project_queries_into`: proj is applied in the key dtype, here fp32).
 //
 // Tile: 128 tokens (MMA M) x L columns (MMA N = L), K = H streamed in 64-column chunks.
-//   A (tokens): cp.async by warps 4-7, 16-byte pieces, into K-major core matrices whose
-//       k-slabs (128 rows x 16 B) sit kPtSlab = 2064 bytes apart: a warp's 32 pieces (4
-//       rows x 128 contiguous bytes in global memory) land in 8 distinct 16-byte bank
-//       groups, so both sides move full-width. Rows past Q are zero-filled.
+//   A (tokens): one TMA tensor copy per stage (box 64 columns x 128 rows, 128-byte swizzle,
+//       K-major: 8-row atoms of 1 KB), rows past Q filled with zeros by the copy.
 //   B (basis): prepared once in core-matrix order per (modality, chunk) by
 //       k_split_basis_tc; one TMA bulk copy per stage brings the three parts.
 //   D: fp32 in tensor memory, [2 buffers][2 modalities][L columns]. A tile runs one MMA
 //       pass per modality present among its tokens; the epilogue (warps 0-3, thread r =
 //       token r, TMEM lane r) picks its token's modality, adds the bias, optionally
 //       L2-normalises (search.py:12-21), and writes qlow (and the typed q_out copy).
-//   warp 8 lane 0 issues the MMAs; barriers: full/empty per stage, full/empty per buffer.
+//   warp 4 lane 0 issues both copies of a stage, warp 8 lane 0 the MMAs; barriers:
+//   full/empty per stage, full/empty per accumulator buffer.
 // Every wait is bounded in time (error bit, stop, bounded drain, TMEM freed).
 #pragma once
+
+#include <cuda.h>
 
 #include <type_traits>
 
@@ -29,8 +30,7 @@
 namespace alut {
 
 constexpr int kPtKc = 64;          // K (H) columns per pipeline stage
-constexpr int kPtSlab = 2064;      // bytes between the A operand's k-slabs (2048 + 16 pad)
-constexpr int kPtThreads = 288;    // warps 0-3 epilogue, 4-7 A loads, 8 MMA
+constexpr int kPtThreads = 288;    // warps 0-3 epilogue, 4 copies, 8 MMA (5-7 idle)
 constexpr int kPtMaxStages = 6;
 constexpr int kPtMinTokens = 256;  // below this the decode-shaped projections are used
 constexpr size_t kPtSmemBudget = 200 * 1024;
@@ -38,7 +38,7 @@ constexpr size_t kPtSmemBudget = 200 * 1024;
 inline bool pt_shape_ok(int l, int h) { return l > 0 && l % 16 == 0 && l <= kTcMaxL && h > 0 && h % kPtKc == 0; }
 // One stage of the basis: three parts x L rows x 64 columns bf16.
 __host__ __device__ inline size_t pt_b_stage_bytes(int l) { return static_cast<size_t>(3) * l * kPtKc * 2; }
-__host__ __device__ inline size_t pt_a_stage_bytes() { return static_cast<size_t>(8) * kPtSlab; }
+__host__ __device__ inline size_t pt_a_stage_bytes() { return static_cast<size_t>(kTcRows) * kPtKc * 2; }
 inline size_t pt_basis_bytes(int l, int h) { return static_cast<size_t>(2) * (h / kPtKc) * pt_b_stage_bytes(l); }
 inline int pt_stages(int l) {
   const size_t st = pt_a_stage_bytes() + pt_b_stage_bytes(l);
@@ -95,6 +95,40 @@ struct PtArgs {
   int* err;
 };
 
+// TMA map of the tokens x [Q][H] bf16 (row stride x_stride elements, a multiple of 8): box
+// 64 columns x 128 rows, 128-byte swizzle, out-of-range rows read as zeros. Returns false if
+// the driver cannot encode it.
+inline bool pt_encode_x_map(CUtensorMap* map, const void* x, int64_t q, int64_t h, int64_t x_stride) {
+  using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static Encode encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qr{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr) != cudaSuccess ||
+        qr != cudaDriverEntryPointSuccess || !fn)
+      return false;
+    encode = reinterpret_cast<Encode>(fn);
+  }
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(h), static_cast<cuuint64_t>(q)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(x_stride) * 2};
+  const cuuint32_t box[2] = {kPtKc, kTcRows};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2D TMA tile load (no multicast): box at (x = column, y = row) of the map into smem.
+__device__ __forceinline__ void pt_tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
 // kind::f16 instruction descriptor: fp32 D, bf16 A and B, K-major, M = 128, N = n.
 __host__ __device__ __forceinline__ uint32_t pt_idesc(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
@@ -108,6 +142,17 @@ __device__ __forceinline__ uint64_t pt_desc(uint32_t saddr, uint32_t lbo, uint32
   d |= static_cast<uint64_t>(1) << 46;
   return d;
 }
+// K-major operand with the 128-byte swizzle: 8-row atoms of 1 KB (SBO), rows of 128 B;
+// within an atom the K offset is added to the start address.
+__device__ __forceinline__ uint64_t pt_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>(1) << 16;           // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;   // SBO: next 8-row atom
+  d |= static_cast<uint64_t>(1) << 46;           // descriptor version
+  d |= static_cast<uint64_t>(2) << 61;           // layout: 128-byte swizzle
+  return d;
+}
 __device__ __forceinline__ void pt_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
@@ -115,14 +160,6 @@ __device__ __forceinline__ void pt_mma(uint32_t tmem, uint64_t da, uint64_t db, 
       "l"(da), "l"(db), "r"(idesc), "r"(acc)
       : "memory");
 }
-// 16-byte cp.async that reads src_bytes (16 or 0) and zero-fills the rest.
-__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
 // tcgen05.ld of W = 32 or 16 consecutive columns of this warp's 32 lanes (warp-collective).
 template <int W>
 __device__ __forceinline__ void tc_ld(uint32_t taddr, float (&v)[W]) {
@@ -151,7 +188,7 @@ __device__ __forceinline__ int pt_tile_mods(const PtArgs& a, int tile) {
   return mods;
 }
 
-__global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(PtArgs a) {
+__global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_constant__ CUtensorMap x_map, PtArgs a) {
   extern __shared__ __align__(1024) unsigned char psm_tc[];
   const int L = a.l;
   const int NS = a.stages;
@@ -180,7 +217,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(PtArgs a) {
   }
   if (tid == 0) {
     for (int i = 0; i < kPtMaxStages; ++i) {
-      mbar_init(&full[i], 128 + 1);  // the A loaders' cp.async arrivals + the basis copy's expect_tx
+      mbar_init(&full[i], 1);  // the producer's expect_tx; both copies complete the bytes
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -197,51 +234,33 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(PtArgs a) {
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
-  if (warp >= 4 && warp < 8) {
-    // ---- loaders: A by cp.async (all 128 threads), B by one bulk copy (thread 128) --------
-    const int pt = tid - 128;
-    int it = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-      const int mods = pt_tile_mods(a, tile);
-      for (int m = 0; m < 2 && ok; ++m) {
-        if (!(mods & (1 << m))) continue;
-        for (int kc = 0; kc < nkc; ++kc, ++it) {
-          const int st = it % NS;
-          if (it >= NS) {
-            bool w = true;
-            if (lane == 0) w = tc_wait(&empty[st], ((it / NS) - 1) & 1, abort_flag);
-            w = __shfl_sync(0xffffffffu, w, 0);
-            if (!w) {
+  if (warp == 4) {
+    // ---- producer: token tile (TMA tensor copy) + basis parts (bulk copy) per stage --------
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int mods = pt_tile_mods(a, tile);
+        for (int m = 0; m < 2 && ok; ++m) {
+          if (!(mods & (1 << m))) continue;
+          for (int kc = 0; kc < nkc; ++kc, ++it) {
+            const int st = it % NS;
+            if (it >= NS && !tc_wait(&empty[st], ((it / NS) - 1) & 1, abort_flag)) {
               ok = false;
               break;
             }
-          }
-          unsigned char* sa = stages + static_cast<size_t>(st) * (a_bytes + b_bytes);
-          const uint32_t sa_addr = smem_addr(sa);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int seg = pt + 128 * i;  // 1024 pieces: (row, k-slab)
-            const int row = (seg & 3) + 4 * (seg >> 5);
-            const int j = (seg >> 2) & 7;
-            const int tok = tile * kTcRows + row;
-            const bool in = tok < a.q;
-            const __nv_bfloat16* src = a.x + (in ? static_cast<int64_t>(tok) * a.x_stride : 0) + kc * kPtKc + j * 8;
-            const uint32_t dst = sa_addr + static_cast<uint32_t>(j * kPtSlab + (row >> 3) * 128 + (row & 7) * 16);
-            cp_async16_zfill(dst, src, in ? 16u : 0u);
-          }
-          cp_async_arrive_noinc(&full[st]);
-          if (pt == 0) {
-            mbar_expect_tx(&full[st], b_bytes);
+            unsigned char* sa = stages + static_cast<size_t>(st) * (a_bytes + b_bytes);
+            mbar_expect_tx(&full[st], a_bytes + b_bytes);
+            pt_tma_load_2d(sa, &x_map, kc * kPtKc, tile * kTcRows, &full[st]);
             bulk_g2s(sa + a_bytes, a.basis + (static_cast<int64_t>(m) * nkc + kc) * b_bytes, b_bytes, &full[st]);
           }
         }
       }
-    }
-    if (pt == 0) s_issued = it;
-    if (!ok && lane == 0 && !*abort_flag) {
-      *abort_flag = 1;
-      atomicOr(a.err, 8);
+      s_issued = it;
+      if (!ok && !*abort_flag) {
+        *abort_flag = 1;
+        atomicOr(a.err, 8);
+      }
     }
   } else if (warp == 8) {
     // ---- MMA issuer ------------------------------------------------------------------------
@@ -266,12 +285,11 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(PtArgs a) {
               ok = false;
               break;
             }
-            fence_async_shared();  // cp.async (generic proxy) writes -> tensor-core reads
             tc_fence_after();
             const uint32_t sa = smem_addr(stages + static_cast<size_t>(st) * (a_bytes + b_bytes));
             const uint32_t sb = sa + a_bytes;
             for (int k16 = 0; k16 < kPtKc / 16; ++k16) {
-              const uint64_t da = pt_desc(sa + k16 * 2 * kPtSlab, kPtSlab, 128);
+              const uint64_t da = pt_desc_sw128(sa + k16 * 32);
 #pragma unroll
               for (int part = 0; part < 3; ++part) {
                 const uint64_t db = pt_desc(sb + part * part_bytes + k16 * 256, 128, kPtKc * 16);
@@ -367,14 +385,11 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(PtArgs a) {
     tc_commit(drain);
     mbar_wait_bounded(drain, 0);
   }
-  if (*abort_flag && tid >= 128 && tid < 256) {
-    asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's own A copies
-    if (tid == 128) {
-      const int issued = s_issued;  // basis copies: the latest use of each stage
-      for (int st = 0; st < NS && st < issued; ++st) {
-        const int last = st + ((issued - 1 - st) / NS) * NS;
-        mbar_wait_bounded(&full[st], (last / NS) & 1);
-      }
+  if (*abort_flag && tid == 128) {
+    const int issued = s_issued;  // copies: the latest use of each stage
+    for (int st = 0; st < NS && st < issued; ++st) {
+      const int last = st + ((issued - 1 - st) / NS) * NS;
+      mbar_wait_bounded(&full[st], (last / NS) & 1);
     }
   }
   __syncthreads();
