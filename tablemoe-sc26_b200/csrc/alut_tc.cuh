@@ -334,25 +334,30 @@ struct TcArgs {
 };
 
 #ifdef ALUT_PHASE_TRACE
-// Development builds: epilogue thread 0 of block 0 sums its waits for the accumulator (slot
-// 40), its filtering (41) and its rescoring (42) in ns; slot 48 counts rescored centroids.
-#define TC_T0() const uint64_t tc_t0_ = global_ns()
-#define TC_ACC(slot) \
-  if (blockIdx.x == 0 && threadIdx.x == 0) g_alut_trace[slot] += global_ns() - tc_t0_
-#define TC_COUNT() \
-  if (blockIdx.x == 0) atomicAdd(&g_alut_trace[48], 1ull)
-#define TC_T0_TID(t) const uint64_t tc_t0_ = (blockIdx.x == 0 && threadIdx.x == (t)) ? global_ns() : 0
-#define TC_ACC_TID(t, slot) \
-  if (blockIdx.x == 0 && threadIdx.x == (t)) g_alut_trace[slot] += global_ns() - tc_t0_
-#define TC_INC_TID(t, slot) \
-  if (blockIdx.x == 0 && threadIdx.x == (t)) g_alut_trace[slot] += 1
+// Development builds: per-thread SM-cycle sums kept in registers (slots 40..55), written once
+// at the end by block 0's epilogue thread 0 (40 accumulator wait, 41 TMEM load, 42 group-end
+// rescoring, 43 filter, 45 slow-path tiles, 46 list overflows, 48 rescored centroids), MMA
+// thread (50 stage wait, 51 accumulator wait) and producer thread (52 stage wait).
+#define TC_TRACE_DECL unsigned long long tc_tr_[16] = {}
+#define TC_T0() const long long tc_t0_ = clock64()
+#define TC_ACC(slot) tc_tr_[(slot) - 40] += static_cast<unsigned long long>(clock64() - tc_t0_)
+#define TC_COUNT() tc_tr_[8] += 1
+#define TC_T0_TID(t) TC_T0()
+#define TC_ACC_TID(t, slot) TC_ACC(slot)
+#define TC_INC_TID(t, slot) tc_tr_[(slot) - 40] += 1
+#define TC_TRACE_FLUSH()                                                                       \
+  if (blockIdx.x == 0 && (tid == 0 || tid == 32 * kTcProducerWarp || tid == 32 * kTcMmaWarp)) \
+    for (int i = 0; i < 16; ++i)                                                               \
+      if (tc_tr_[i]) g_alut_trace[40 + i] += tc_tr_[i]
 #else
+#define TC_TRACE_DECL do {} while (0)
 #define TC_T0() do {} while (0)
 #define TC_ACC(slot) do {} while (0)
 #define TC_COUNT() do {} while (0)
 #define TC_T0_TID(t) do {} while (0)
 #define TC_ACC_TID(t, slot) do {} while (0)
 #define TC_INC_TID(t, slot) do {} while (0)
+#define TC_TRACE_FLUSH() do {} while (0)
 #endif
 
 __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
@@ -376,6 +381,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
   __shared__ int s_abort, s_issued, s_groups_issued;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   volatile int* abort_flag = &s_abort;
+  TC_TRACE_DECL;
 
   const int ntiles = a.meta[0] * a.nchunks;
   const int t_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * ntiles / gridDim.x);
@@ -415,9 +421,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
     // ---- producer --------------------------------------------------------------------------
     if (lane == 0) {
       int gi = -1, prev = -1, it = 0, table = 0;
+      int g = t_begin / a.nchunks, c = t_begin - g * a.nchunks;  // advanced without divisions
+      int st = 0, wrapped = 0;                                      // stage, and its reuse parity
       bool ok = true;
       for (int tile = t_begin; tile < t_end && ok; ++tile, ++it) {
-        const int g = tile / a.nchunks, c = tile % a.nchunks;
         if (g != prev) {
           table = a.groups[g].x;
           const int ab = (gi + 1) & 1;
@@ -430,11 +437,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
           mbar_expect_tx(&a_full[ab], tb);
           bulk_g2s(sA + ab * tb, a.qsplit + static_cast<int64_t>(g) * tb, tb, &a_full[ab]);
         }
-        const int st = it % NS;
         bool w;
         {
           TC_T0_TID(32 * kTcProducerWarp);
-          w = it < NS || tc_wait(&empty[st], ((it / NS) - 1) & 1, abort_flag);
+          w = it < NS || tc_wait(&empty[st], wrapped ^ 1, abort_flag);  // use it - NS done
           TC_ACC_TID(32 * kTcProducerWarp, 52);
         }
         if (!w) {
@@ -443,6 +449,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
         }
         mbar_expect_tx(&full[st], tb);
         bulk_g2s(sK + st * tb, a.ksplit + (static_cast<int64_t>(table) * a.nchunks + c) * tb, tb, &full[st]);
+        if (++st == NS) {
+          st = 0;
+          wrapped ^= 1;
+        }
+        if (++c == a.nchunks) {
+          c = 0;
+          ++g;
+        }
       }
       s_issued = it;
       s_groups_issued = gi + 1;
@@ -455,9 +469,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
     // ---- MMA issuer ------------------------------------------------------------------------
     if (lane == 0) {
       int gi = -1, prev = -1, it = 0;
+      int g = t_begin / a.nchunks, c = t_begin - g * a.nchunks;
+      int st = 0, sph = 0;  // stage and the parity of its current use
       bool ok = true;
       for (int tile = t_begin; tile < t_end; ++tile, ++it) {
-        const int g = tile / a.nchunks;
         if (g != prev) {
           prev = g;
           ++gi;
@@ -466,11 +481,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
             break;
           }
         }
-        const int st = it % NS, acc = it % kTcAcc;
+        const int acc = it % kTcAcc;
         bool w1, w2;
         {
           TC_T0_TID(32 * kTcMmaWarp);
-          w1 = tc_wait(&full[st], (it / NS) & 1, abort_flag);
+          w1 = tc_wait(&full[st], sph, abort_flag);
           TC_ACC_TID(32 * kTcMmaWarp, 50);
         }
         {
@@ -485,11 +500,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
         tc_fence_after();
         const uint32_t a0 = smem_addr(sA + (gi & 1) * tb), b0 = smem_addr(sK + st * tb);
         const uint32_t d = tmem + static_cast<uint32_t>(acc * kTcRows);
-        for (int ks = 0; ks < L / 16; ++ks)
-          tc_mma(d, tc_desc(a0 + ks * 256, L), tc_desc(b0 + ks * 256, L), ks > 0);
+        if (L == 128) {
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) tc_mma(d, tc_desc(a0 + ks * 256, 128), tc_desc(b0 + ks * 256, 128), ks > 0);
+        } else if (L == 64) {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) tc_mma(d, tc_desc(a0 + ks * 256, 64), tc_desc(b0 + ks * 256, 64), ks > 0);
+        } else {
+          for (int ks = 0; ks < L / 16; ++ks) tc_mma(d, tc_desc(a0 + ks * 256, L), tc_desc(b0 + ks * 256, L), ks > 0);
+        }
         tc_commit(&empty[st]);
         tc_commit(&t_full[acc]);
-        if (tile + 1 == t_end || (tile + 1) / a.nchunks != g) tc_commit(&a_empty[gi & 1]);
+        if (tile + 1 == t_end || c == a.nchunks - 1) tc_commit(&a_empty[gi & 1]);
+        if (++st == NS) {
+          st = 0;
+          sph ^= 1;
+        }
+        if (++c == a.nchunks) {
+          c = 0;
+          ++g;
+        }
       }
       if (!ok && !*abort_flag) {
         *abort_flag = 1;
@@ -507,8 +537,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
     float amax = -INFINITY, tw = 0.f;
     const float* q = nullptr;
     const float* kt = nullptr;
-    for (int tile = t_begin; tile < t_end; ++tile, ++it) {
-      const int g = tile / a.nchunks, c = tile - g * a.nchunks;
+    int g = t_begin / a.nchunks, c = t_begin - g * a.nchunks;
+    for (int tile = t_begin; tile < t_end; ++tile, ++it, (++c == a.nchunks ? (c = 0, ++g) : 0)) {
       if (g != prev) {
         prev = g;
         const int4 gg = a.groups[g];
@@ -570,10 +600,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
           // Qualifying columns as bit masks (predicated compares, no branches), then one
           // insertion per set bit - usually one.
           uint32_t mk0 = 0u, mk1 = 0u;
+          if (m0 >= thr) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            mk0 |= (v[j] >= thr ? 1u : 0u) << j;
-            mk1 |= (v[32 + j] >= thr ? 1u : 0u) << j;
+            for (int j = 0; j < 32; ++j) mk0 |= (v[j] >= thr ? 1u : 0u) << j;
+          }
+          if (m1 >= thr) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) mk1 |= (v[32 + j] >= thr ? 1u : 0u) << j;
           }
           const uint64_t mk = (static_cast<uint64_t>(mk1) << 32) | mk0;
           // The stored value: with one qualifying column it is the slice maximum itself; with
@@ -591,7 +624,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
           }
         }
         TC_ACC(43);
-        if (tile + 1 == t_end || (tile + 1) / a.nchunks != g) {
+        if (tile + 1 == t_end || c == a.nchunks - 1) {
           TC_T0();
           unsigned long long mine = s_mine[e];
           for (int i = 0; i < n; ++i) {
@@ -627,6 +660,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       mbar_wait_bounded(&a_full[ab], (last >> 1) & 1);
     }
   }
+  TC_TRACE_FLUSH();
   __syncthreads();
   if (warp == kTcMmaWarp)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
