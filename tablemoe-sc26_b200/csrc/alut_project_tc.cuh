@@ -237,15 +237,14 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
   if (warp == 4) {
     // ---- producer: token tile (TMA tensor copy) + basis parts (bulk copy) per stage --------
     if (lane == 0) {
-      int it = 0;
+      int it = 0, st = 0, wrapped = 0;  // stage and the parity of its reuse, without divisions
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
         const int mods = pt_tile_mods(a, tile);
         for (int m = 0; m < 2 && ok; ++m) {
           if (!(mods & (1 << m))) continue;
-          for (int kc = 0; kc < nkc; ++kc, ++it) {
-            const int st = it % NS;
-            if (it >= NS && !tc_wait(&empty[st], ((it / NS) - 1) & 1, abort_flag)) {
+          for (int kc = 0; kc < nkc; ++kc, ++it, (++st == NS ? (st = 0, wrapped ^= 1) : 0)) {
+            if (it >= NS && !tc_wait(&empty[st], wrapped ^ 1, abort_flag)) {
               ok = false;
               break;
             }
@@ -265,7 +264,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
   } else if (warp == 8) {
     // ---- MMA issuer ------------------------------------------------------------------------
     if (lane == 0) {
-      int it = 0, tc = 0;
+      int it = 0, tc = 0, st = 0, sph = 0;
       bool ok = true;
       const uint32_t idesc = pt_idesc(L);
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++tc) {
@@ -279,9 +278,8 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
         for (int m = 0; m < 2 && ok; ++m) {
           if (!(mods & (1 << m))) continue;
           const uint32_t d = tmem + static_cast<uint32_t>((buf * 2 + m) * L);
-          for (int kc = 0; kc < nkc; ++kc, ++it) {
-            const int st = it % NS;
-            if (!tc_wait(&full[st], (it / NS) & 1, abort_flag)) {
+          for (int kc = 0; kc < nkc; ++kc, ++it, (++st == NS ? (st = 0, sph ^= 1) : 0)) {
+            if (!tc_wait(&full[st], sph, abort_flag)) {
               ok = false;
               break;
             }
