@@ -320,7 +320,10 @@ static int launch_plan(const ProjPlanArgs& a, int* tabs, cudaStream_t st) {
     k_plan_count<<<grid, 256, hs, st>>>(a, tabs);
     rc = check_launch("k_plan_count");
     if (rc) return rc;
-    k_plan_groups<<<1, kProjThreads, 0, st>>>(a, tabs, tabs + ntab);
+    const size_t gs = sizeof(int) * (ntab + 1);
+    rc = allow_smem(reinterpret_cast<const void*>(k_plan_groups), gs);
+    if (rc) return rc;
+    k_plan_groups<<<1, kProjThreads, gs, st>>>(a, tabs, tabs + ntab);
     rc = check_launch("k_plan_groups");
     if (rc) return rc;
     k_plan_scatter<<<grid, 256, 0, st>>>(a, tabs + ntab);

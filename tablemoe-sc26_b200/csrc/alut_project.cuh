@@ -210,9 +210,11 @@ __global__ void __launch_bounds__(256) k_plan_count(ProjPlanArgs a, int* counts)
 }
 
 __global__ void __launch_bounds__(kProjThreads) k_plan_groups(ProjPlanArgs a, const int* counts, int* offs) {
+  extern __shared__ __align__(16) int pg_smem[];  // [ntab + 1] first group of each table
   const int tid = threadIdx.x;
   const int G = a.group > 0 ? a.group : kSearchGroup;
   const int ntab = 2 * a.num_experts;
+  int* gstart = pg_smem;
   __shared__ int scan_scratch[kProjThreads];
   __shared__ int s_tot_c, s_tot_g;
   const int per = (ntab + kProjThreads - 1) / kProjThreads;
@@ -227,12 +229,26 @@ __global__ void __launch_bounds__(kProjThreads) k_plan_groups(ProjPlanArgs a, co
   int bg = block_exclusive_scan_256(lg, scan_scratch, &s_tot_g);
   for (int t = t0; t < t1; ++t) {
     offs[t] = bc;
-    const int c = counts[t];
-    for (int g = 0; g * G < c; ++g) a.groups[bg + g] = make_int4(t, bc + g * G, min(G, c - g * G), 0);
-    bc += c;
-    bg += (c + G - 1) / G;
+    gstart[t] = bg;
+    bc += counts[t];
+    bg += (counts[t] + G - 1) / G;
   }
-  if (tid == 0) a.meta[0] = s_tot_g;
+  if (tid == 0) {
+    gstart[ntab] = s_tot_g;
+    a.meta[0] = s_tot_g;
+  }
+  __syncthreads();
+  // Groups in parallel: group gi belongs to the last table whose first group is <= gi (never
+  // an empty table: its first group equals the next table's).
+  for (int gi = tid; gi < s_tot_g; gi += kProjThreads) {
+    int lo = 0, hi = ntab;  // gstart[lo] <= gi < gstart[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (gstart[mid] <= gi) lo = mid; else hi = mid;
+    }
+    const int k = gi - gstart[lo];
+    a.groups[gi] = make_int4(lo, offs[lo] + k * G, min(G, counts[lo] - k * G), 0);
+  }
 }
 
 __global__ void __launch_bounds__(256) k_plan_scatter(ProjPlanArgs a, int* offs) {

@@ -136,14 +136,22 @@ __global__ void k_stage_queries(const float* qlow, int L, int s, const int* sort
   const int units = L / 8;
   const int64_t ngroups = min(static_cast<int64_t>(meta[0]), max_groups);
   const int64_t total = ngroups * kTcRows * units;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+  // When L / 8 is a power of two the threads of a row are an aligned group of adjacent lanes
+  // and reduce the squared norm with shuffles; otherwise the row's first thread sums it.
+  const bool pow2 = (units & (units - 1)) == 0;
+  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x - (threadIdx.x & 31); i0 < total;
+       i0 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = i0 + (threadIdx.x & 31);  // whole warps iterate together (shuffles)
+    const bool live = i < total;
     const int u = static_cast<int>(i % units);
     const int r = static_cast<int>((i / units) % kTcRows);
     const int64_t g = i / (static_cast<int64_t>(units) * kTcRows);
-    const int4 gg = groups[g];
-    const int p = r < gg.z ? sorted[gg.y + r] : -1;
-    const float* qrow = p >= 0 ? qlow + static_cast<int64_t>(p / s) * L : nullptr;
+    const float* qrow = nullptr;
+    if (live) {
+      const int4 gg = groups[g];
+      const int p = r < gg.z ? sorted[gg.y + r] : -1;
+      qrow = p >= 0 ? qlow + static_cast<int64_t>(p / s) * L : nullptr;
+    }
     float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (qrow) {
       const float4 a = *reinterpret_cast<const float4*>(qrow + u * 8);
@@ -151,16 +159,23 @@ __global__ void k_stage_queries(const float* qlow, int L, int s, const int* sort
       v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
       v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     }
+    float ss = 0.f;
     __align__(16) __nv_bfloat16 h[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) h[j] = __float2bfloat16_rn(v[j]);
-    unsigned char* base = reinterpret_cast<unsigned char*>(qsplit) + g * tc_tile_bytes(L);
-    *reinterpret_cast<uint4*>(base + tc_off(r, u * 8, L)) = *reinterpret_cast<const uint4*>(h);
-    if (u == 0) {
-      float ss = 0.f;
-      if (qrow)
-        for (int k = 0; k < L; ++k) ss = fmaf(qrow[k], qrow[k], ss);
-      qnorm[g * kTcRows + r] = sqrtf(ss);
+    for (int j = 0; j < 8; ++j) {
+      h[j] = __float2bfloat16_rn(v[j]);
+      ss = fmaf(v[j], v[j], ss);
+    }
+    if (pow2) {
+      for (int o = units >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    } else if (u == 0 && qrow) {
+      ss = 0.f;
+      for (int k = 0; k < L; ++k) ss = fmaf(qrow[k], qrow[k], ss);
+    }
+    if (live) {
+      unsigned char* base = reinterpret_cast<unsigned char*>(qsplit) + g * tc_tile_bytes(L);
+      *reinterpret_cast<uint4*>(base + tc_off(r, u * 8, L)) = *reinterpret_cast<const uint4*>(h);
+      if (u == 0) qnorm[g * kTcRows + r] = sqrtf(ss);
     }
   }
 }
