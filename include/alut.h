@@ -223,6 +223,20 @@ int alut_merge_packed(int32_t world, int32_t q, int32_t s, const uint64_t* packe
                       const uint8_t* is_vision, const alut_search_params_t* params,
                       uint8_t* out_hit, int64_t* out_idx, alut_stream_t stream);
 
+/* a6: the online window lookup of the hybrid decode search (search.py:778-806). x [b,h]
+ * (x_dtype, row stride x_stride) against the window's first n_valid keys [.,h] (key_dtype
+ * == x_dtype, row stride key_stride, 16-byte aligned): scores rounded to that dtype (the
+ * reference's matmul output dtype), first index of the maximum, valid iff > 0. eids [.,t]
+ * int64 (row stride t) are the window's cached expert ids; target [b,s] (row stride
+ * target_stride) the experts of the slots searched online. Writes on_idx[b] (-1 if
+ * invalid), on_hit [b,s] u8 and on_slot [b,s] int64 (row stride out_stride elements each):
+ * on_hit = valid and target among eids[on_idx]; on_slot = its first position, 0 without a
+ * hit (the reference leaves those untouched in buffers its callers pre-zero). */
+int alut_online_search(int32_t b, int32_t h, int32_t n_valid, int32_t t, int32_t s, const void* x,
+                       int32_t x_dtype, int64_t x_stride, const void* keys, int32_t key_dtype, int64_t key_stride,
+                       const int64_t* eids, const int64_t* target, int64_t target_stride, uint8_t* on_hit,
+                       int64_t* on_idx, int64_t* on_slot, int64_t out_stride, alut_stream_t stream);
+
 /* ---- peer access for the centroid-range shards (new; no reference counterpart) ----------
  * Each rank exports the device allocation holding its value slice as a CUDA IPC handle
  * (ALUT_PEER_HANDLE_BYTES bytes, plus the slice's offset inside the allocation), the

@@ -8,7 +8,8 @@ imports or calls it.
 The C functions restate the reference's torch path (fanyalun/tablemoe-sc26):
 ``search.py:476-498`` projection, ``search.py:566-602`` / ``:661-697`` search,
 ``manager.py:212`` gather and ``cached_layers.py:455-465`` + ``skip/pruning.py:55-73``
-combine. See ``alut_oracle.c`` for the per-function citations.
+combine. See ``alut_oracle.c`` for the per-function citations. ``online_search`` (numpy)
+restates the online window lookup, ``search.py:778-806``.
 """
 from __future__ import annotations
 
@@ -181,3 +182,26 @@ def bf16_to_f32(bits):
 
 if os.environ.get("ALUT_ORACLE_REBUILD"):
     build(force=True)
+
+
+def online_search(x_bits, key_bits, eids, target, n_valid):
+    """The online window lookup (search.py:778-806, ``_search_decode_online_into``).
+
+    x_bits [B,H] and key_bits [N,H] are bf16 bit patterns (the model dtype). Scores are
+    the matmul of the two in bf16 - accumulated in fp32, rounded to bf16 - over the first
+    n_valid window entries; per token the first index of the maximum; a token is valid iff
+    its maximum is > 0 (then on_idx = that index, else -1). For each target expert id
+    target[b, s]: on_hit = valid and the id is among eids[on_idx]; on_slot = the first
+    position of the id there (0 where no hit). Returns (on_hit, on_idx, on_slot, scores).
+    """
+    x = bf16_to_f32(np.asarray(x_bits)).reshape(np.shape(x_bits))
+    k = bf16_to_f32(np.asarray(key_bits)).reshape(np.shape(key_bits))[:n_valid]
+    scores = bf16_to_f32(bf16_bits((x @ k.T).astype(np.float32))).reshape(x.shape[0], -1)
+    arg = scores.argmax(axis=1)  # first index of the maximum
+    valid = scores[np.arange(x.shape[0]), arg] > 0
+    on_idx = np.where(valid, arg, -1).astype(np.int64)
+    cached = np.asarray(eids)[arg]                              # [B, T]
+    match = np.asarray(target)[:, :, None] == cached[:, None, :]  # [B, S, T]
+    on_hit = match.any(-1) & valid[:, None]
+    on_slot = np.where(on_hit, match.argmax(-1), 0).astype(np.int64)
+    return on_hit, on_idx, on_slot, scores

@@ -16,6 +16,7 @@
 #include "alut_tc.cuh"
 #include "alut_project_tc.cuh"
 #include "alut_peer.cuh"
+#include "alut_online.cuh"
 
 namespace alut {
 
@@ -613,6 +614,47 @@ int alut_debug_trace(unsigned long long* host, int n) {
   return cudaMemcpyFromSymbol(host, g_alut_trace, sizeof(unsigned long long) * (n < 64 ? n : 64)) == cudaSuccess ? 0 : -4;
 }
 #endif
+
+int alut_online_search(int32_t b, int32_t h, int32_t n_valid, int32_t t, int32_t s, const void* x,
+                       int32_t x_dtype, int64_t x_stride, const void* keys, int32_t key_dtype, int64_t key_stride,
+                       const int64_t* eids, const int64_t* target, int64_t target_stride, uint8_t* on_hit,
+                       int64_t* on_idx, int64_t* on_slot, int64_t out_stride, alut_stream_t stream) {
+  if (b < 0 || h <= 0 || n_valid < 0 || t < 0 || s < 0) return fail(ALUT_EINVAL, "online_search: sizes");
+  if (b == 0) return ALUT_OK;
+  if (!x || !on_hit || !on_idx || !on_slot || (n_valid > 0 && (!keys || !eids)) || (s > 0 && !target))
+    return fail(ALUT_EINVAL, "online_search: NULL argument");
+  if (!dtype_ok(x_dtype) || x_dtype != key_dtype)
+    return fail(ALUT_EDTYPE, "online_search: x and the window must share one dtype");
+  const int esz = dtype_size(key_dtype);
+  if (h > kOnlineMaxH || (h * esz) % 16 != 0 || x_stride < h || key_stride < h || (key_stride * esz) % 16 != 0 ||
+      !aligned16(keys) || out_stride < s || target_stride < s)
+    return fail(ALUT_ESHAPE, "online_search: h=%d must fill 16-byte units (<= %d), strides", h, kOnlineMaxH);
+  OnlineArgs a{b, h, n_valid, t, s, x, x_stride, keys, key_stride, eids, target, target_stride, on_hit, on_idx,
+               on_slot, out_stride};
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t smem = sizeof(float) * h;
+  switch (key_dtype) {
+    case ALUT_F32: {
+      int rc = allow_smem(reinterpret_cast<const void*>(k_online_search<float>), smem);
+      if (rc) return rc;
+      k_online_search<float><<<b, kOnlineThreads, smem, st>>>(a);
+      break;
+    }
+    case ALUT_BF16: {
+      int rc = allow_smem(reinterpret_cast<const void*>(k_online_search<__nv_bfloat16>), smem);
+      if (rc) return rc;
+      k_online_search<__nv_bfloat16><<<b, kOnlineThreads, smem, st>>>(a);
+      break;
+    }
+    case ALUT_F16: {
+      int rc = allow_smem(reinterpret_cast<const void*>(k_online_search<__half>), smem);
+      if (rc) return rc;
+      k_online_search<__half><<<b, kOnlineThreads, smem, st>>>(a);
+      break;
+    }
+  }
+  return check_launch("k_online_search");
+}
 
 // ---- peer access for the centroid-range shards (CUDA IPC; no multicast objects) -------------
 

@@ -83,6 +83,8 @@ SIGNATURES = {
                                                    _I32, _P, _P, _I64, _P]),
     "alut_search_packed": (ctypes.c_int, [_TP, _BP, _PP, _P, _I64, _P, _P, _SZ, _P]),
     "alut_merge_packed": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _PP, _P, _P, _P]),
+    "alut_online_search": (ctypes.c_int, [_I32, _I32, _I32, _I32, _I32, _P, _I32, _I64, _P, _I32, _I64, _P, _P,
+                                          _I64, _P, _P, _P, _I64, _P]),
     "alut_peer_export": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_uint64)]),
     "alut_peer_open": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]),
     "alut_peer_close": (ctypes.c_int, [_P, ctypes.c_uint64]),

@@ -179,20 +179,31 @@ class VectorSearchEngine:
         return m.online_size if m.online_full else m.online_ptr
 
     def _search_online_into(self, hidden_states, target_eids, out_on_hit, out_on_idx, out_on_slot):
-        """Online window lookup (search.py:778-806): best of the recent tokens by raw dot
-        product, then the first cached slot holding the target expert."""
+        """Online window lookup (search.py:778-806) in one kernel (``alut_online_search``):
+        best of the recent tokens by dot product in the window dtype, valid iff > 0, then
+        the first cached slot holding each target expert."""
         n = self._online_valid_size()
         if n == 0 or target_eids.shape[1] == 0:
             return False
-        keys = self.manager.online_keys[:n]
-        eids = self.manager.online_expert_ids[:n]
-        best, arg = torch.matmul(hidden_states, keys.transpose(0, 1)).max(dim=1)
-        ok = best > 0
-        out_on_idx.copy_(torch.where(ok, arg, out_on_idx))
-        match = target_eids.unsqueeze(-1) == eids[arg].unsqueeze(1)
-        hits = match.any(dim=-1) & ok.unsqueeze(1)
-        out_on_hit.copy_(hits)
-        out_on_slot.copy_(torch.where(hits, match.int().argmax(dim=-1), out_on_slot))
+        keys = self.manager.online_keys
+        eids = self.manager.online_expert_ids
+        x = hidden_states if hidden_states.stride(-1) == 1 else hidden_states.contiguous()
+        if x.dtype != keys.dtype:
+            x = x.to(keys.dtype)
+        tgt = target_eids if target_eids.dtype == torch.int64 else target_eids.long()
+        if tgt.stride(-1) != 1:
+            tgt = tgt.contiguous()
+        if eids.dtype != torch.int64 or not eids.is_contiguous() or keys.stride(-1) != 1:
+            raise ValueError("online window: keys [N,H] with unit inner stride, expert ids int64 [N,T] contiguous")
+        if out_on_hit.stride() != out_on_slot.stride() or out_on_hit.stride(-1) != 1:
+            raise ValueError("online outputs: on_hit / on_slot must share strides with unit inner stride")
+        bs, s = tgt.shape
+        rc = self._lib.alut_online_search(bs, x.shape[-1], n, eids.shape[1], s, x.data_ptr(), _alut.dtype_code(x.dtype),
+                                          x.stride(0), keys.data_ptr(), _alut.dtype_code(keys.dtype), keys.stride(0),
+                                          eids.data_ptr(), tgt.data_ptr(), tgt.stride(0), out_on_hit.data_ptr(),
+                                          out_on_idx.data_ptr(), out_on_slot.data_ptr(), out_on_hit.stride(0),
+                                          _alut.stream_ptr(self.device))
+        _alut.check(rc, "alut_online_search")
         return True
 
     def search_decode_hybrid(self, layer_idx, hidden_states, selected_experts, is_vision_mask, keep_k=None):

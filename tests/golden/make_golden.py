@@ -152,6 +152,52 @@ def make_case(ref, name, *, Q, S, E, K, L, H, dtype, variant, seed, vis_frac=0.5
     return meta
 
 
+def online_case(ref, name, *, B, H, size, topk_online, S, keep_k, n_valid, full, seed, dup=False,
+                 negative=False, match_p=0.5):
+    """The online window lookup (search.py:778-806, ``_search_decode_online_into``): bf16
+    hidden states against the window's bf16 keys, first-index argmax, valid iff > 0, then
+    the first cached slot holding each target expert."""
+    search_mod, _, _ = ref
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, H, generator=g).to(torch.bfloat16)
+    keys = torch.randn(size, H, generator=g).to(torch.bfloat16)
+    if negative:  # every score < 0: no valid token
+        keys = (-x.float().mean(0, keepdim=True).sign() * keys.float().abs()).to(torch.bfloat16)
+    if dup:  # duplicate window entries: the first index must win
+        keys[3] = keys[1]
+        keys[7 % size] = keys[2]
+        x[0] = keys[1]
+        x[1] = keys[2]
+    eids = torch.randint(0, 10, (size, topk_online), generator=g)
+    eids[torch.rand(size, topk_online, generator=g) < 0.15] = -1
+    sel = torch.randint(0, 10, (B, S), generator=g)
+    # Route some target experts to ids present in the best window entry, so that slots hit.
+    scores = (x.float() @ keys.float().T)[:, :n_valid]
+    arg = scores.argmax(1)
+    for b in range(B):
+        for s in range(keep_k, S):
+            if torch.rand(1, generator=g).item() < match_p:
+                cand = eids[arg[b]][eids[arg[b]] >= 0]
+                if cand.numel():
+                    sel[b, s] = cand[int(torch.randint(0, cand.numel(), (1,), generator=g))]
+    mgr = SyntheticManager(torch.zeros(1, 2, 1, 1), torch.zeros(1, 2, 1, 1),
+                           {m: {"proj": torch.eye(1), "bias": torch.zeros(1)} for m in ("vision", "text")},
+                           torch.zeros(1, 2, 1, 1, dtype=torch.bfloat16))
+    mgr.online_keys, mgr.online_expert_ids = keys, eids
+    mgr.online_size, mgr.online_full, mgr.online_ptr = size, full, (0 if full else n_valid)
+    eng = search_mod.VectorSearchEngine(mgr)
+    on_hit = torch.zeros(B, S - keep_k, dtype=torch.bool)
+    on_idx = torch.full((B,), -1, dtype=torch.long)
+    on_slot = torch.zeros(B, S - keep_k, dtype=torch.long)
+    has = eng._search_decode_online_into(x, sel[:, keep_k:], on_hit, on_idx, on_slot)
+    out = dict(x_bf16=_bits(x), keys_bf16=_bits(keys), eids=eids.numpy(), sel=sel.numpy(),
+               on_hit=on_hit.numpy().astype(np.uint8), on_idx=on_idx.numpy(), on_slot=on_slot.numpy())
+    meta = dict(name=name, B=B, H=H, size=size, topk_online=topk_online, S=S, keep_k=keep_k,
+                n_valid=n_valid, full=full, has_online=bool(has))
+    np.savez_compressed(HERE / f"online_{name}.npz", meta=json.dumps(meta), **out)
+    print(f"online_{name}: valid={int((on_idx >= 0).sum())}/{B} hits={int(on_hit.sum())}")
+
+
 def known_answer(ref):
     """The reference's own known-answer tests (test_search.py:36-89) as vectors."""
     search_mod, _, _ = ref
@@ -211,6 +257,15 @@ def main():
               variant="decode_dot", seed=10, reuse_p=0.6, dot_thr=9.0)
     make_case(ref, "ragged_l12_k7", Q=5, S=3, E=4, K=7, L=12, H=40, dtype="float32",
               variant="prefill_dot", seed=9, reuse_p=0.7)
+    # The online window (ONLINE_CACHE_SIZE 64, ONLINE_TOP_K 6, config.py:29-30).
+    online_case(ref, "full64", B=16, H=256, size=64, topk_online=6, S=8, keep_k=3, n_valid=64, full=True,
+                seed=40)
+    online_case(ref, "partial5_bs1", B=1, H=2048, size=64, topk_online=6, S=8, keep_k=2, n_valid=5, full=False,
+                seed=41, match_p=0.8)
+    online_case(ref, "ties", B=4, H=128, size=16, topk_online=6, S=6, keep_k=1, n_valid=16, full=True, seed=42,
+                dup=True)
+    online_case(ref, "negative", B=4, H=64, size=8, topk_online=6, S=4, keep_k=1, n_valid=8, full=True, seed=43,
+                negative=True)
 
 
 if __name__ == "__main__":

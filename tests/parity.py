@@ -28,7 +28,18 @@ ULP = {"float32": 2.0 ** -23, "bfloat16": 2.0 ** -8, "float16": 2.0 ** -11}
 
 
 def golden_names():
-    return sorted(p.stem for p in GOLDEN.glob("*.npz"))
+    """Search/combine fixtures (the online-window fixtures are online_*.npz)."""
+    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("online_"))
+
+
+def online_names():
+    return sorted(p.stem for p in GOLDEN.glob("online_*.npz"))
+
+
+def load_online(name):
+    z = np.load(GOLDEN / f"{name}.npz")
+    meta = json.loads(str(z["meta"]))
+    return meta, {k: z[k] for k in z.files if k != "meta"}
 
 
 def load_golden(name):
@@ -109,3 +120,24 @@ def check_combined(got, ref, what=""):
     err = np.abs(got - ref)
     tol = COMBINE_RTOL * np.abs(ref) + COMBINE_RTOL * scale + 1e-12
     assert np.all(err <= tol), f"{what}: combine max err {err.max()} (scale {scale})"
+
+
+def check_online(got_hit, got_idx, got_slot, ref_hit, ref_idx, ref_slot, scores, what=""):
+    """Online-window parity: exact, except for a token whose two best bf16 scores lie within
+    2 bf16 ulp of each other (fp32 accumulation order): there the chosen entry's score must
+    be within that tolerance of the best, and its hits follow the chosen entry."""
+    got_hit, ref_hit = np.asarray(got_hit).astype(bool), np.asarray(ref_hit).astype(bool)
+    got_idx, ref_idx = np.asarray(got_idx), np.asarray(ref_idx)
+    bad = []
+    for b in range(len(ref_idx)):
+        if got_idx[b] == ref_idx[b]:
+            if not (np.array_equal(got_hit[b], ref_hit[b]) and
+                    np.array_equal(np.where(ref_hit[b], got_slot[b], 0), np.where(ref_hit[b], ref_slot[b], 0))):
+                bad.append((b, "hits/slots"))
+            continue
+        best = scores[b].max()
+        chosen = scores[b, got_idx[b]] if got_idx[b] >= 0 else -np.inf
+        tol = 2 * ULP["bfloat16"] * max(abs(best), 1e-30)
+        if got_idx[b] < 0 or ref_idx[b] < 0 or abs(best - chosen) > tol:
+            bad.append((b, "idx", int(got_idx[b]), int(ref_idx[b])))
+    assert not bad, f"{what}: {bad[:5]}"

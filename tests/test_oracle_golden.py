@@ -7,7 +7,8 @@ import numpy as np
 import pytest
 
 import oracle.oracle as orc
-from parity import GOLDEN, case_inputs, check_combined, check_search, golden_names, load_golden
+from parity import (GOLDEN, case_inputs, check_combined, check_online, check_search, golden_names, load_golden,
+                    load_online, online_names)
 
 
 @pytest.mark.parametrize("name", golden_names())
@@ -69,3 +70,13 @@ def test_oracle_zero_query_normalises_to_zero():
     proj = np.random.default_rng(0).standard_normal((2, 8, 4)).astype(np.float32)
     q = orc.project(x, np.array([1, 0], np.uint8), proj, np.zeros((2, 4), np.float32), normalize=True)
     assert np.all(q == 0)
+
+
+@pytest.mark.parametrize("name", online_names())
+def test_oracle_online_window_matches_reference(name):
+    """search.py:778-806 against the reference's own outputs (online_*.npz)."""
+    meta, d = load_online(name)
+    keep = meta["keep_k"]
+    hit, idx, slot, scores = orc.online_search(d["x_bf16"], d["keys_bf16"], d["eids"], d["sel"][:, keep:],
+                                               meta["n_valid"])
+    check_online(hit, idx, slot, d["on_hit"], d["on_idx"], d["on_slot"], scores, what=name)
