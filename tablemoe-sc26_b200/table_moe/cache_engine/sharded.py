@@ -186,6 +186,15 @@ class ShardedCentroidTable:
             return self._peers is not False
         lib = _alut.load()
         v = self.values
+        if self.world == 1:  # the one slice is local: no handles to exchange
+            if not (v.is_contiguous() and v.shape[0] == 1):
+                self._peers = False
+                return False
+            dev = self.device
+            self._peers = (torch.tensor([v.data_ptr()], dtype=torch.int64, device=dev),
+                           torch.tensor([self.k0, self.k1], dtype=torch.int64, device=dev),
+                           torch.tensor([v.stride(1)], dtype=torch.int64, device=dev), [], v.stride(2))
+            return True
         ok = v.is_contiguous() and v.shape[0] == 1
         handle = (ctypes.c_ubyte * _alut.PEER_HANDLE_BYTES)()
         off = ctypes.c_uint64(0)
@@ -216,7 +225,7 @@ class ShardedCentroidTable:
     def close(self):
         """Unmap the peers' value slices (collective: every rank calls it before freeing its
         values, so that no peer still reads them)."""
-        if self._peers:
+        if self._peers and self.world > 1:
             torch.cuda.synchronize(self.device)
             dist.barrier(group=self.group)
             lib = _alut.load()
@@ -258,7 +267,8 @@ class ShardedCentroidTable:
         if self.world > 1 and q % self.world:
             raise ValueError(f"token count {q} is not a multiple of the world size {self.world}")
         hit, idx = self.search(x, is_vision)
-        if self._nccl() and self.gather_owned == self._gather_owned and self._peer_setup():
+        direct = self.world == 1 and self.device.type == "cuda"
+        if (direct or self._nccl()) and self.gather_owned == self._gather_owned and self._peer_setup():
             lo, hi = q * self.rank // self.world, q * (self.rank + 1) // self.world
             return hit, idx, self._gather_peer(hit, idx, is_vision, lo, hi)
         rows = self.gather_owned(hit, idx, is_vision)
