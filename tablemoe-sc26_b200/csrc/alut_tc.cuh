@@ -288,6 +288,12 @@ __device__ __forceinline__ float tc_exact(const float* q, const float* kp, int L
   return e;
 }
 
+// L2 prefetch of a row of L fp32 values (whole 128-byte lines), so that a later exact
+// rescoring of it finds it on chip.
+__device__ __forceinline__ void tc_prefetch_row(const float* p, int L) {
+  for (int o = 0; o < L; o += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + o));
+}
+
 // Packed exact candidate of centroid row kr (out of line: rare, and register-hungry).
 __device__ __noinline__ unsigned long long tc_rescore(const float* q, const float* kt, int64_t sk, int L, int kr,
                                                       uint32_t idx_offset) {
@@ -568,6 +574,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
           q = a.qlow + static_cast<int64_t>(p / a.s) * L;
           kt = a.keys + static_cast<int64_t>(table >> 1) * a.key_stride_e +
                static_cast<int64_t>(table & 1) * a.key_stride_m;
+          if (half == 0) tc_prefetch_row(q, L);
         }
       }
       const int acc = it % kTcAcc;
@@ -636,6 +643,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
             s_cc[n * kTcEpiThreads + e] = kb + j;
             s_cv[n * kTcEpiThreads + e] = x;
             ++n;
+            tc_prefetch_row(kt + static_cast<int64_t>(kb + j) * a.key_stride_k, L);
           }
         }
         TC_ACC(43);
