@@ -287,7 +287,29 @@ static int launch_project(int key_dtype, int x_dtype, const ProjPlanArgs& a, cud
     int rc = allow_smem(reinterpret_cast<const void*>(k_project_tc), sm);
     if (rc) return rc;
     const int ntiles = ceil_div(a.q, kTcRows);
-    k_project_tc<<<std::min(ntiles, num_sms()), kPtThreads, sm, st>>>(x_map, p);
+    const int sms = num_sms();
+    // Few tiles: split H over a cluster of up to 8 CTAs per tile.
+    int ksplit = 1;
+    while (ksplit < 8 && ntiles * ksplit * 2 <= sms && ksplit * 2 <= a.h / kPtKc) ksplit *= 2;
+    p.ksplit = ksplit;
+    if (ksplit == 1) {
+      k_project_tc<<<std::min(ntiles, sms), kPtThreads, sm, st>>>(x_map, p);
+      return check_launch("k_project_tc");
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ntiles * ksplit);
+    cfg.blockDim = dim3(kPtThreads);
+    cfg.dynamicSmemBytes = sm;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = ksplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_project_tc, x_map, p);
+    if (e != cudaSuccess) return fail(ALUT_ECUDA, "k_project_tc (cluster of %d): %s", ksplit, cudaGetErrorString(e));
     return check_launch("k_project_tc");
   }
   if (mma_projection_ok(key_dtype, x_dtype, a)) {

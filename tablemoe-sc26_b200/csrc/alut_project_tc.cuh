@@ -16,12 +16,19 @@
 //       L2-normalises (search.py:12-21), and writes qlow (and the typed q_out copy).
 //   warp 4 lane 0 issues both copies of a stage, warp 8 lane 0 the MMAs; barriers:
 //   full/empty per stage, full/empty per accumulator buffer.
+// Few token tiles (fewer than half the SMs): H is split over a thread-block cluster of
+// ksplit CTAs per tile. Each runs the pipeline over its share of the 64-column stages and
+// leaves its fp32 partial rows in its own shared memory; after a cluster barrier the
+// leader sums the partials over distributed shared memory in rank order (deterministic)
+// and finishes the rows; a second barrier keeps the peers' memory alive until then.
 // Every wait is bounded in time (error bit, stop, bounded drain, TMEM freed).
 #pragma once
 
 #include <cuda.h>
 
 #include <type_traits>
+
+#include <cooperative_groups.h>
 
 #include "alut_common.cuh"
 #include "alut_project.cuh"
@@ -88,6 +95,7 @@ struct PtArgs {
   const unsigned char* basis;  // k_split_basis_tc layout
   const float* bias[2];
   int q, h, l, stages, normalize;
+  int ksplit;  // CTAs per token tile (a cluster) splitting H; 1 = persistent CTAs over tiles
   float eps;
   float* qlow;
   float* q_out;  // optional fp32 copy with its own row stride
@@ -207,7 +215,14 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
   volatile int* abort_flag = &s_abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ntiles = (a.q + kTcRows - 1) / kTcRows;
-  if (static_cast<int>(blockIdx.x) >= ntiles) return;
+  const bool split = a.ksplit > 1;
+  // Tiles this CTA runs (tile0, tile0 + tstep, ...) and its stages [kc0, kc1) of each.
+  const int rank = split ? static_cast<int>(blockIdx.x) % a.ksplit : 0;
+  const int tile0 = split ? static_cast<int>(blockIdx.x) / a.ksplit : static_cast<int>(blockIdx.x);
+  const int tstep = split ? ntiles : static_cast<int>(gridDim.x);
+  const int kc0 = split ? rank * nkc / a.ksplit : 0;
+  const int kc1 = split ? (rank + 1) * nkc / a.ksplit : nkc;
+  if (!split && tile0 >= ntiles) return;  // (split grids are exactly ntiles x ksplit)
   const uint32_t ncols = pt_tmem_cols(L);
   if (warp == 8) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
@@ -239,11 +254,11 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
     if (lane == 0) {
       int it = 0, st = 0, wrapped = 0;  // stage and the parity of its reuse, without divisions
       bool ok = true;
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+      for (int tile = tile0; tile < ntiles && ok; tile += tstep) {
         const int mods = pt_tile_mods(a, tile);
         for (int m = 0; m < 2 && ok; ++m) {
           if (!(mods & (1 << m))) continue;
-          for (int kc = 0; kc < nkc; ++kc, ++it, (++st == NS ? (st = 0, wrapped ^= 1) : 0)) {
+          for (int kc = kc0; kc < kc1; ++kc, ++it, (++st == NS ? (st = 0, wrapped ^= 1) : 0)) {
             if (it >= NS && !tc_wait(&empty[st], wrapped ^ 1, abort_flag)) {
               ok = false;
               break;
@@ -267,7 +282,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
       int it = 0, tc = 0, st = 0, sph = 0;
       bool ok = true;
       const uint32_t idesc = pt_idesc(L);
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++tc) {
+      for (int tile = tile0; tile < ntiles && ok; tile += tstep, ++tc) {
         const int mods = pt_tile_mods(a, tile);
         const int buf = tc & 1;
         if (tc >= 2 && !tc_wait(&t_empty[buf], ((tc >> 1) - 1) & 1, abort_flag)) {
@@ -278,7 +293,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
         for (int m = 0; m < 2 && ok; ++m) {
           if (!(mods & (1 << m))) continue;
           const uint32_t d = tmem + static_cast<uint32_t>((buf * 2 + m) * L);
-          for (int kc = 0; kc < nkc; ++kc, ++it, (++st == NS ? (st = 0, sph ^= 1) : 0)) {
+          for (int kc = kc0; kc < kc1; ++kc, ++it, (++st == NS ? (st = 0, sph ^= 1) : 0)) {
             if (!tc_wait(&full[st], sph, abort_flag)) {
               ok = false;
               break;
@@ -291,7 +306,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
 #pragma unroll
               for (int part = 0; part < 3; ++part) {
                 const uint64_t db = pt_desc(sb + part * part_bytes + k16 * 256, 128, kPtKc * 16);
-                pt_mma(d, da, db, idesc, (kc | k16 | part) != 0);
+                pt_mma(d, da, db, idesc, (kc != kc0 || k16 != 0 || part != 0) ? 1u : 0u);
               }
             }
             tc_commit(&empty[st]);
@@ -309,7 +324,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
     const int r = tid;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     int tc = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
+    for (int tile = tile0; tile < ntiles; tile += tstep, ++tc) {
       const int mods = pt_tile_mods(a, tile);
       const int buf = tc & 1;
       const bool ok = tc_wait(&t_full[buf], (tc >> 1) & 1, abort_flag);
@@ -326,6 +341,27 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
       const int mr = valid && !a.is_vision[tok] ? 1 : 0;
       // Section of this lane's modality; when both are present every lane loads both.
       const int m_only = mods == 2 ? 1 : 0;
+      if (split) {  // this CTA's share of H: park the row's partial sums for the leader
+        float* part = reinterpret_cast<float*>(stages) + static_cast<size_t>(r) * (L + 4);
+        for (int c0 = 0; c0 < L; c0 += 16) {
+          float v[16];
+          __syncwarp();
+          tc_ld<16>(lane_base + static_cast<uint32_t>((buf * 2 + m_only) * L + c0), v);
+          if (mods == 3) {
+            float w[16];
+            tc_ld<16>(lane_base + static_cast<uint32_t>((buf * 2 + 1) * L + c0), w);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = mr ? w[j] : v[j];
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            reinterpret_cast<float4*>(part + c0)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&t_empty[buf]);
+        continue;
+      }
       const float* bias = a.bias[valid ? mr : m_only];
       float denom = 1.f;
       bool zero = false;
@@ -379,6 +415,66 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
   }
 
   __syncthreads();
+  if (split) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();  // every rank's partial rows are in its shared memory
+    if (rank == 0 && tid < kTcRows) {
+      const int r = tid;
+      const int tok = tile0 * kTcRows + r;
+      if (tok < a.q) {
+        const int mr = a.is_vision[tok] ? 0 : 1;
+        const float* bias = a.bias[mr];
+        float denom = 1.f;
+        bool zero = false;
+        for (int pass = a.normalize ? 0 : 1; pass < 2; ++pass) {
+          float ss = 0.f;
+          for (int c0 = 0; c0 < L; c0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0.f;
+            for (int k = 0; k < a.ksplit; ++k) {  // rank order: the same sum on every run
+              const float* pk = cluster.map_shared_rank(reinterpret_cast<float*>(stages), k) +
+                                static_cast<size_t>(r) * (L + 4) + c0;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 f = reinterpret_cast<const float4*>(pk)[j];
+                v[4 * j] += f.x;
+                v[4 * j + 1] += f.y;
+                v[4 * j + 2] += f.z;
+                v[4 * j + 3] += f.w;
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += __ldg(bias + c0 + j);
+            if (pass == 0) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) ss = fmaf(v[j], v[j], ss);
+            } else {
+              if (a.normalize) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = zero ? 0.f : v[j] / denom;
+              }
+              float4* dst = reinterpret_cast<float4*>(a.qlow + static_cast<int64_t>(tok) * L + c0);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              if (a.q_out) {
+                float* o = a.q_out + static_cast<int64_t>(tok) * a.q_out_stride + c0;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) o[j] = v[j];
+              }
+            }
+          }
+          if (pass == 0) {
+            const float n = sqrtf(ss);
+            denom = fmaxf(n, a.eps);
+            zero = n <= a.eps;
+          }
+        }
+      }
+    }
+    cluster.sync();  // the leader has read every rank's partials
+  }
   if (*abort_flag && tid == 32 * 8) {
     tc_commit(drain);
     mbar_wait_bounded(drain, 0);

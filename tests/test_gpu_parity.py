@@ -225,6 +225,7 @@ def test_projection_matches_oracle():
     (4096, 2048, 64, "first1024", True),  # C3-like: image tokens first, pure tiles
     (300, 512, 128, "mixed", True),      # ragged last tile, L = 128
     (777, 256, 48, "none", False),       # L = 48, text only
+    (12000, 256, 64, "mixed", False),    # 94 tiles: persistent CTAs, no H split
 ])
 def test_large_batch_projection_matches_oracle(Q, H, L, vis, normalize):
     """bf16 tokens, fp32 basis, >= 256 tokens: the tcgen05 projection (128-token tiles, basis
