@@ -132,7 +132,20 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
     }
-    for (int i = 0; i < n; ++i) {
+    // Four rows' loads in flight before their FMAs, which still run in slot order.
+    int i = 0;
+    for (; i + 4 <= n; i += 4) {
+      float v[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) load8<TV>(vals + s_offl[i + u] + h0, v[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float w = s_wl[i + u];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = fmaf(w, v[u][j], acc[j]);
+      }
+    }
+    for (; i < n; ++i) {
       float v[8];
       load8<TV>(vals + s_offl[i] + h0, v);
       const float w = s_wl[i];
