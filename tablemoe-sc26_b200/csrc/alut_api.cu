@@ -74,8 +74,7 @@ static int num_sms() {
 
 // Raise a kernel's dynamic shared memory limit once per (kernel, device).
 static int allow_smem(const void* kernel, size_t bytes) {
-  // Dynamic shared memory above the 48 KB default (counting the kernel's static shared
-  // memory) needs an opt-in; the table remembers each (kernel, device, size) it checked.
+  if (bytes <= 48 * 1024) return ALUT_OK;
   struct Entry { const void* k; int dev; int bytes; };
   static Entry table[256];
   static int used = 0;
@@ -86,13 +85,9 @@ static int allow_smem(const void* kernel, size_t bytes) {
   for (int i = 0; i < used; ++i)
     if (table[i].k == kernel && table[i].dev == dev && table[i].bytes >= static_cast<int>(bytes))
       return ALUT_OK;
-  cudaFuncAttributes fa;
-  cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
-  if (e != cudaSuccess) return fail(ALUT_ECUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
-  if (bytes + fa.sharedSizeBytes > 48 * 1024) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
-    if (e != cudaSuccess) return fail(ALUT_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  }
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(bytes));
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   if (used < 256) table[used++] = Entry{kernel, dev, static_cast<int>(bytes)};
   return ALUT_OK;
 }
@@ -321,7 +316,7 @@ static int launch_project(int key_dtype, int x_dtype, const ProjPlanArgs& a, cud
     // The cluster size may drop to 8 inside launch_project_kernel; size for the larger layout.
     const size_t sm = std::max(mma_smem_layout(a.l, a.h, a.nsplit).total,
                                mma_smem_layout(a.l, a.h, std::min(a.nsplit, 8)).total);
-    return launch_project_kernel(k_project_mma<float, false>, a, sm, st);
+    return launch_project_kernel(k_project_mma<float>, a, sm, st);
   }
   switch (key_dtype) {
     case ALUT_F32: return launch_project_k<float>(x_dtype, a, smem, st);
@@ -329,26 +324,6 @@ static int launch_project(int key_dtype, int x_dtype, const ProjPlanArgs& a, cud
     case ALUT_F16: return launch_project_k<__half>(x_dtype, a, smem, st);
   }
   return fail(ALUT_EDTYPE, "key dtype");
-}
-
-// Splits of H for the decode projection without a cluster: a power of two <=
-// kMaxPartialSplit with at least kPartialMinKSteps 16-wide k-steps per split.
-constexpr int kPartialMinKSteps = 8;
-static int decode_splits(int h) {
-  int s = 1;
-  while (s * 2 <= kMaxPartialSplit && (h / 16) / (s * 2) >= kPartialMinKSteps) s *= 2;
-  return s;
-}
-
-// Decode projection without the cluster: k_project_mma<float, true> stores partial rows.
-static int launch_project_partial(const ProjPlanArgs& a, cudaStream_t st) {
-  const size_t sm = mma_smem_layout(a.l, a.h, a.nsplit).total;
-  auto kern = k_project_mma<float, true>;
-  int rc = allow_smem(reinterpret_cast<const void*>(kern), sm);
-  if (rc) return rc;
-  cudaError_t e = launch_pdl(kern, dim3(a.qtiles * a.nsplit), dim3(kProjThreads), sm, st, a);
-  if (e != cudaSuccess) return fail(ALUT_ECUDA, "k_project_mma (partial): %s", cudaGetErrorString(e));
-  return check_launch("k_project_mma");
 }
 
 // Slots above which the plan runs over the whole GPU (three launches) instead of one CTA.
@@ -434,34 +409,21 @@ static int launch_combine_t(bool vec, const CombineArgs& a, dim3 grid, cudaStrea
   return check_launch("k_combine");
 }
 
-template <typename TK, typename TV, bool kFuse>
+template <typename TK>
 static int launch_search_decode_t(const DecodeScanArgs& d, dim3 grid, size_t smem, cudaStream_t st) {
-  auto kern = k_search_decode<TK, TV, kFuse>;
-  int rc = allow_smem(reinterpret_cast<const void*>(kern), smem);
+  int rc = allow_smem(reinterpret_cast<const void*>(k_search_decode<TK>), smem);
   if (rc) return rc;
-  cudaError_t e = launch_pdl(kern, grid, dim3(kSearchThreads), smem, st, d);
+  cudaError_t e = launch_pdl(k_search_decode<TK>, grid, dim3(kSearchThreads), smem, st, d);
   if (e != cudaSuccess) return fail(ALUT_ECUDA, "k_search_decode: %s", cudaGetErrorString(e));
   return check_launch("k_search_decode");
 }
 
-template <typename TK>
-static int launch_search_decode_k(int fuse_dtype, const DecodeScanArgs& d, dim3 grid, size_t smem,
-                                  cudaStream_t st) {
-  switch (fuse_dtype) {
-    case -1: return launch_search_decode_t<TK, __nv_bfloat16, false>(d, grid, smem, st);
-    case ALUT_BF16: return launch_search_decode_t<TK, __nv_bfloat16, true>(d, grid, smem, st);
-    case ALUT_F16: return launch_search_decode_t<TK, __half, true>(d, grid, smem, st);
-  }
-  return fail(ALUT_EDTYPE, "fused combine dtype");
-}
-
-// fuse_dtype: -1 for the scan alone, else the value (= output) dtype of the fused combine.
-static int launch_search_decode(int key_dtype, int fuse_dtype, const DecodeScanArgs& d, dim3 grid, size_t smem,
+static int launch_search_decode(int key_dtype, const DecodeScanArgs& d, dim3 grid, size_t smem,
                                 cudaStream_t st) {
   switch (key_dtype) {
-    case ALUT_F32: return launch_search_decode_k<float>(fuse_dtype, d, grid, smem, st);
-    case ALUT_BF16: return launch_search_decode_k<__nv_bfloat16>(fuse_dtype, d, grid, smem, st);
-    case ALUT_F16: return launch_search_decode_k<__half>(fuse_dtype, d, grid, smem, st);
+    case ALUT_F32: return launch_search_decode_t<float>(d, grid, smem, st);
+    case ALUT_BF16: return launch_search_decode_t<__nv_bfloat16>(d, grid, smem, st);
+    case ALUT_F16: return launch_search_decode_t<__half>(d, grid, smem, st);
   }
   return fail(ALUT_EDTYPE, "key dtype");
 }
@@ -476,15 +438,10 @@ static int launch_combine(int vd, int od, bool vec, const CombineArgs& a, dim3 g
   return fail(ALUT_EDTYPE, "combine: value dtype %d with out dtype %d not supported", vd, od);
 }
 
-// Projection + plan + centroid scan into the packed best buffer `best`. With `fuse` (the
-// combine of alut_lookup_combine, whose value and output dtypes are `fuse_dtype`), a decode
-// batch also runs the combine inside the scan kernel and sets *fused; otherwise the caller
-// launches the combine.
+// Projection + plan + centroid scan into the packed best buffer `best`.
 static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_search_params_t* p,
                       const void* keys, const void* q_low_in, uint32_t idx_offset,
-                      uint64_t* best, void* workspace, size_t ws_bytes, cudaStream_t st,
-                      const CombineArgs* fuse = nullptr, int fuse_dtype = -1, bool* fused = nullptr) {
-  if (fused) *fused = false;
+                      uint64_t* best, void* workspace, size_t ws_bytes, cudaStream_t st) {
   const Workspace w = workspace_layout(b->q, b->s, t->l, 2 * t->num_experts);
   if (!workspace) return fail(ALUT_EWORKSPACE, "workspace is NULL");
   if (ws_bytes < w.total)
@@ -532,35 +489,9 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     a.zero_best = best;
     a.zero_n = pairs;
     if (g_prof_start && g_prof_stop && record_profile(g_prof_start, st)) return ALUT_ECUDA;
-    // bf16 tokens on an fp32 basis: the tensor-core projection stores per-split partial
-    // rows, which the scan sums (no cluster reduction between the two kernels).
-    const bool partial = mma_projection_ok(t->key_dtype, b->x_dtype, a) && t->l <= kMaxL;
-    int rc;
-    if (partial) {
-      a.nsplit = decode_splits(t->h);
-      a.qpart = reinterpret_cast<float*>(base + w.qpart);
-      a.zero_cnt = reinterpret_cast<int*>(base + w.tokcnt);
-      a.zero_cnt_n = b->q;
-      rc = launch_project_partial(a, st);
-    } else {
-      rc = launch_project(t->key_dtype, b->x_dtype, a, st);
-    }
+    int rc = launch_project(t->key_dtype, b->x_dtype, a, st);
     if (rc) return rc;
     DecodeScanArgs d{};
-    if (partial) {
-      d.qpart = a.qpart;
-      d.nsplit = a.nsplit;
-      d.normalize = a.normalize;
-      d.eps = a.eps;
-      d.bias[0] = static_cast<const float*>(a.bias[0]);
-      d.bias[1] = static_cast<const float*>(a.bias[1]);
-      if (fuse) {
-        d.tokcnt = a.zero_cnt;
-        d.c = *fuse;
-        d.c.best = best;
-      }
-    }
-    const int fd = (partial && fuse) ? fuse_dtype : -1;
     d.s.keys = keys;
     d.s.key_stride_e = t->key_stride[0];
     d.s.key_stride_m = t->key_stride[1];
@@ -580,9 +511,8 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     d.reuse = b->reuse;
     d.reuse_stride = b->reuse_stride;
     d.err = a.meta + 1;
-    rc = launch_search_decode(t->key_dtype, fd, d, dim3(pairs, d.s.nchunks), search_decode_smem_bytes(t->l, esz), st);
+    rc = launch_search_decode(t->key_dtype, d, dim3(pairs, d.s.nchunks), search_decode_smem_bytes(t->l, esz), st);
     if (rc) return rc;
-    if (fused) *fused = fd >= 0;
     if (g_prof_start && g_prof_stop && record_profile(g_prof_stop, st)) return ALUT_ECUDA;
     return ALUT_OK;
   }
@@ -716,6 +646,7 @@ int alut_debug_trace_reset(void) {
     hi[i] = 0ull;
   }
   if (cudaMemcpyToSymbol(g_alut_trace_lo, lo, sizeof(lo)) != cudaSuccess) return -4;
+  if (cudaMemcpyToSymbol(g_alut_trace, hi, sizeof(hi)) != cudaSuccess) return -4;
   return cudaMemcpyToSymbol(g_alut_trace_hi, hi, sizeof(hi)) == cudaSuccess ? 0 : -4;
 }
 #endif
@@ -1092,6 +1023,8 @@ int alut_lookup_combine(const alut_tables_t* tables, const alut_batch_t* batch,
   if (!workspace || workspace_bytes < w.total)
     return fail(ALUT_EWORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, w.total);
   uint64_t* best = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + w.best);
+  rc = run_search(tables, batch, params, keys, nullptr, 0u, best, workspace, workspace_bytes, st);
+  if (rc) return rc;
   CombineArgs c{};
   fill_value_strides(tables, c);
   c.q = batch->q;
@@ -1116,15 +1049,9 @@ int alut_lookup_combine(const alut_tables_t* tables, const alut_batch_t* batch,
   c.out_hit = out_hit;
   c.out_idx = out_idx;
   c.out_hit_stride = out_stride_hit;
-  const bool vec = combine_vec(tables, out, out_stride, out_dtype);
-  const int fuse_dtype = (vec && tables->value_dtype == out_dtype &&
-                          (out_dtype == ALUT_BF16 || out_dtype == ALUT_F16)) ? out_dtype : -1;
-  bool fused = false;
-  rc = run_search(tables, batch, params, keys, nullptr, 0u, best, workspace, workspace_bytes, st,
-                  fuse_dtype >= 0 ? &c : nullptr, fuse_dtype, &fused);
-  if (rc || fused) return rc;
   dim3 grid(batch->q, ceil_div(tables->h, kCombineSpan));
-  return launch_combine(tables->value_dtype, out_dtype, vec, c, grid, st);
+  return launch_combine(tables->value_dtype, out_dtype, combine_vec(tables, out, out_stride, out_dtype),
+                        c, grid, st);
 }
 
 int alut_search_packed(const alut_tables_t* tables, const alut_batch_t* batch,

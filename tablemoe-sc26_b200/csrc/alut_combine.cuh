@@ -41,37 +41,43 @@ struct CombineArgs {
 constexpr int kCombineSpan = kCombineThreads * 8;
 static_assert(kMaxSlots <= kCombineThreads, "one slot per thread in the combine prologue");
 
-// Shared memory of one token's combine.
-struct CombineSmem {
-  float w[kMaxSlots];
-  uint8_t surv[kMaxSlots];
-  uint8_t look[kMaxSlots];
-  int64_t off[kMaxSlots];
-  float wl[kMaxSlots];
-  int64_t offl[kMaxSlots];
-  int n;
-};
-
-// One token's combine by the whole CTA: hit rule per slot (from the packed best, read past
-// L1 because other CTAs wrote it with atomics), survivor renormalisation, then the weighted
-// fp32 sum of the looked-up rows in slot order over columns [h_begin, h_end), 8 per thread
-// per pass. Ends with a barrier, so `sm` may be reused for the next token. Not inlined: the
-// decode scan calls it only in the CTAs that complete a token.
 template <typename TV, typename TO, bool kVec>
-__device__ __noinline__ void combine_token(const CombineArgs& a, int t, int64_t h_begin, int64_t h_end,
-                                           bool write_hits, CombineSmem& sm) {
-  const int tid = threadIdx.x, nthr = blockDim.x;
+__global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
+  __shared__ float s_w[kMaxSlots];
+  __shared__ uint8_t s_surv[kMaxSlots];
+  __shared__ uint8_t s_look[kMaxSlots];
+  __shared__ int64_t s_off[kMaxSlots];
+  __shared__ float s_wl[kMaxSlots];
+  __shared__ int64_t s_offl[kMaxSlots];
+  __shared__ int s_n;
+  const int tid = threadIdx.x;
+  const int t = blockIdx.x;
+  ALUT_TRACE(20);
+  pdl_launch_dependents();
+  // Inputs first (they do not depend on the search), then wait for the search results.
+  bool r_ = false, ev_ = false, comp_ = false;
+  int64_t e_ = 0;
+  float w_ = 0.f;
   const int m = a.is_vision[t] ? 0 : 1;
-  for (int s = tid; s < a.s; s += nthr) {
-    const bool r = a.reuse ? (a.reuse[t * a.reuse_stride + s] != 0) : true;
-    const int64_t e = a.sel[t * a.sel_stride + s];
-    const bool ev = e >= 0 && e < a.num_experts;
+  if (tid < a.s) {
+    r_ = a.reuse ? (a.reuse[t * a.reuse_stride + tid] != 0) : true;
+    e_ = a.sel[t * a.sel_stride + tid];
+    ev_ = e_ >= 0 && e_ < a.num_experts;
+    comp_ = a.compute ? (a.compute[t * a.compute_stride + tid] != 0) : false;
+    w_ = a.w[t * a.w_stride + tid];
+  }
+  ALUT_TRACE(21);
+  pdl_wait();
+  ALUT_TRACE(22);
+  for (int s = tid; s < a.s; s += kCombineThreads) {
+    const bool r = r_;
+    const int64_t e = e_;
+    const bool ev = ev_;
     bool hit = false;
     int64_t idx = 0;
     if (a.best) {
       if (r && ev) {
-        const uint64_t b =
-            __ldcg(reinterpret_cast<const unsigned long long*>(a.best) + static_cast<int64_t>(t) * a.s + s);
+        const uint64_t b = a.best[static_cast<int64_t>(t) * a.s + s];
         if (b) {
           hit = hit_rule(cand_score(b), m == 0 ? a.thr_vis : a.thr_txt, a.cmp_ge);
           if (hit) idx = cand_index(b);
@@ -81,98 +87,83 @@ __device__ __noinline__ void combine_token(const CombineArgs& a, int t, int64_t 
       hit = r && a.hit_in[t * a.hit_stride + s] != 0;
       idx = a.idx_in[t * a.hit_stride + s];
     }
-    if (a.out_hit && write_hits) {
+    if (a.out_hit && blockIdx.y == 0) {
       a.out_hit[t * a.out_hit_stride + s] = hit ? 1 : 0;
       a.out_idx[t * a.out_hit_stride + s] = hit ? idx : 0;
     }
-    const bool comp = a.compute ? (a.compute[t * a.compute_stride + s] != 0) : false;
+    const bool comp = comp_;
     const bool look = hit && ev && idx >= 0 && idx < a.k;
-    sm.w[s] = a.w[t * a.w_stride + s];
-    sm.surv[s] = (comp || hit) ? 1 : 0;
-    sm.look[s] = look ? 1 : 0;
-    sm.off[s] = look ? (e * a.vs_e + m * a.vs_m + idx * a.vs_k) : 0;
+    s_w[s] = w_;
+    s_surv[s] = (comp || hit) ? 1 : 0;
+    s_look[s] = look ? 1 : 0;
+    s_off[s] = look ? (e * a.vs_e + m * a.vs_m + idx * a.vs_k) : 0;
   }
   __syncthreads();
   if (tid == 0) {
     float kept = 0.f, tot = 0.f;
     for (int s = 0; s < a.s; ++s) {
-      kept += sm.surv[s] ? sm.w[s] : 0.f;
-      tot += sm.w[s];
+      kept += s_surv[s] ? s_w[s] : 0.f;
+      tot += s_w[s];
     }
     int n = 0;
     for (int s = 0; s < a.s; ++s) {
-      if (!sm.look[s]) continue;
-      float w = sm.w[s];
+      if (!s_look[s]) continue;
+      float w = s_w[s];
       if (a.renorm == ALUT_RENORM_TO_ONE) w = kept > 0.f ? w / kept : 0.f;
       else if (a.renorm == ALUT_RENORM_TO_ROWSUM) w = kept > 0.f ? (w / kept) * tot : 0.f;
-      sm.wl[n] = w;
-      sm.offl[n] = sm.off[s];
+      s_wl[n] = w;
+      s_offl[n] = s_off[s];
       ++n;
     }
-    sm.n = n;
+    s_n = n;
   }
   __syncthreads();
   ALUT_TRACE(23);
-  if (a.out) {
-    const int n = sm.n;
-    const TV* vals = static_cast<const TV*>(a.values);
-    for (int64_t h0 = h_begin + static_cast<int64_t>(tid) * 8; h0 < h_end; h0 += static_cast<int64_t>(nthr) * 8) {
-      TO* out = static_cast<TO*>(a.out) + static_cast<int64_t>(t) * a.out_stride + h0;
-      float acc[8];
-      if (kVec) {
-        if (a.accumulate) load8_rw<TO>(out, acc);
-        else {
+  if (!a.out) return;
+  const int n = s_n;
+  const int64_t h0 = static_cast<int64_t>(blockIdx.y) * kCombineSpan + tid * 8;
+  if (h0 >= a.h) return;
+  TO* out = static_cast<TO*>(a.out) + static_cast<int64_t>(t) * a.out_stride + h0;
+  const TV* vals = static_cast<const TV*>(a.values);
+  float acc[8];
+  if (kVec) {
+    if (a.accumulate) load8_rw<TO>(out, acc);
+    else {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-        }
-        // Four rows' loads in flight before their FMAs, which still run in slot order.
-        int i = 0;
-        for (; i + 4 <= n; i += 4) {
-          float v[4][8];
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    }
+    // Four rows' loads in flight before their FMAs, which still run in slot order.
+    int i = 0;
+    for (; i + 4 <= n; i += 4) {
+      float v[4][8];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) load8<TV>(vals + sm.offl[i + u] + h0, v[u]);
+      for (int u = 0; u < 4; ++u) load8<TV>(vals + s_offl[i + u] + h0, v[u]);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float w = sm.wl[i + u];
+      for (int u = 0; u < 4; ++u) {
+        const float w = s_wl[i + u];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] = fmaf(w, v[u][j], acc[j]);
-          }
-        }
-        for (; i < n; ++i) {
-          float v[8];
-          load8<TV>(vals + sm.offl[i] + h0, v);
-          const float w = sm.wl[i];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] = fmaf(w, v[j], acc[j]);
-        }
-        store8<TO>(out, acc);
-      } else {
-        const int64_t rem = h_end - h0;
-        const int cnt = rem < 8 ? static_cast<int>(rem) : 8;
-        for (int j = 0; j < cnt; ++j) acc[j] = a.accumulate ? to_f32<TO>(out[j]) : 0.f;
-        for (int i = 0; i < n; ++i) {
-          const float w = sm.wl[i];
-          for (int j = 0; j < cnt; ++j) acc[j] = fmaf(w, to_f32<TV>(vals[sm.offl[i] + h0 + j]), acc[j]);
-        }
-        for (int j = 0; j < cnt; ++j) out[j] = from_f32<TO>(acc[j]);
+        for (int j = 0; j < 8; ++j) acc[j] = fmaf(w, v[u][j], acc[j]);
       }
     }
+    for (; i < n; ++i) {
+      float v[8];
+      load8<TV>(vals + s_offl[i] + h0, v);
+      const float w = s_wl[i];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = fmaf(w, v[j], acc[j]);
+    }
+    store8<TO>(out, acc);
+    ALUT_TRACE(24);
+  } else {
+    const int64_t rem = a.h - h0;
+    const int cnt = rem < 8 ? static_cast<int>(rem) : 8;
+    for (int j = 0; j < cnt; ++j) acc[j] = a.accumulate ? to_f32<TO>(out[j]) : 0.f;
+    for (int i = 0; i < n; ++i) {
+      const float w = s_wl[i];
+      for (int j = 0; j < cnt; ++j) acc[j] = fmaf(w, to_f32<TV>(vals[s_offl[i] + h0 + j]), acc[j]);
+    }
+    for (int j = 0; j < cnt; ++j) out[j] = from_f32<TO>(acc[j]);
   }
-  ALUT_TRACE(24);
-  __syncthreads();
-}
-
-// Stand-alone combine: one CTA per (token, 512-column slice).
-template <typename TV, typename TO, bool kVec>
-__global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
-  __shared__ CombineSmem sm;
-  ALUT_TRACE(20);
-  pdl_launch_dependents();
-  pdl_wait();
-  ALUT_TRACE(22);
-  const int64_t h0 = static_cast<int64_t>(blockIdx.y) * kCombineSpan;
-  const int64_t h1 = h0 + kCombineSpan < a.h ? h0 + kCombineSpan : a.h;
-  combine_token<TV, TO, kVec>(a, blockIdx.x, h0, h1, blockIdx.y == 0, sm);
 }
 
 // Bit-exact copy of value rows (manager.py:212-228). Rows are moved as 16-byte words

@@ -21,8 +21,6 @@ constexpr int kSearchChunkK = kSearchThreads;
 constexpr int kSearchGroup = 32;         // (token, slot) pairs scored per search tile
 constexpr int kMaxTables = 4096;         // 2 * num_experts
 constexpr int kMaxSlots = 64;            // top_k
-constexpr int kDecodeMaxPairs = 256;     // decode scan: (token, slot) pairs of one batch
-constexpr int kDecodeMaxTokens = 32;
 constexpr int kCombineThreads = 64;      // 8 elements per thread -> 512 per CTA
 constexpr int kProjSplitTarget = 296;    // 2 CTAs per SM over 148 SMs
 
@@ -215,10 +213,6 @@ struct Workspace {
   // staged per group of <= 128 slots as bf16 operand tiles, and their norms.
   size_t qsplit;    // bf16   [tc_groups][128 * L]
   size_t qnorm;     // f32    [tc_groups][128]
-  // Decode batches (Q <= kDecodeMaxTokens): the projection's per-split partial rows and
-  // the per-token completion counters of the fused combine.
-  size_t qpart;     // f32    [qtiles][kMaxPartialSplit][16][L]  (qtiles of min(Q, 32) tokens)
-  size_t tokcnt;    // int32  [min(Q, 32)]
   size_t total;
   int64_t max_groups;
   int64_t tc_groups;
@@ -232,7 +226,6 @@ inline int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) 
 // (the split CTAs form one thread-block cluster) when the batch is small, so that a decode
 // batch still spreads its projection over several SMs; 1 for large batches.
 constexpr int kMaxClusterSplit = 16;  // a non-portable cluster size, allowed on sm_100
-constexpr int kMaxPartialSplit = 32;  // decode projection without a cluster (partial rows)
 inline int proj_splits(int q, int h) {
   const int qtiles = ceil_div(q, kProjTileQ);
   int cap = kProjSplitTarget / (qtiles > 0 ? qtiles : 1);
@@ -255,13 +248,6 @@ inline Workspace workspace_layout(int q, int s, int l, int num_tables, bool tc =
   w.sorted = off;   off = align256(off + sizeof(int32_t) * (pairs + 1));
   w.groups = off;   off = align256(off + sizeof(int4) * w.max_groups);
   w.tabs = off;     off = align256(off + sizeof(int32_t) * 2 * num_tables);
-  {
-    // Sized for min(q, kDecodeMaxTokens) tokens, so that the total never shrinks as q grows.
-    const int qd = q < kDecodeMaxTokens ? q : kDecodeMaxTokens;
-    w.qpart = off;  off = align256(off + sizeof(float) * static_cast<size_t>(ceil_div(qd, kProjTileQ)) *
-                                            kMaxPartialSplit * kProjTileQ * l);
-    w.tokcnt = off; off = align256(off + sizeof(int32_t) * (qd + 1));
-  }
   if (tc) {
     // Groups of <= 128 slots of one table (this bound is below max_groups, which the plan's
     // group list uses in both cases).

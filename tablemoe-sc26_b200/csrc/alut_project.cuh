@@ -36,12 +36,6 @@ struct ProjPlanArgs {
   // decode path: clear best[0, zero_n) for the scan that follows
   uint64_t* zero_best;
   int zero_n;
-  // decode path without the cluster reduction: each split CTA stores its partial rows to
-  // qpart[(qtile * nsplit + split) * 16 + row][L] (k_project_mma<.., true>); CTA 0 also
-  // clears the per-token completion counters zero_cnt[0, zero_cnt_n) of the fused combine
-  float* qpart;
-  int* zero_cnt;
-  int zero_cnt_n;
   // plan
   int s;
   int num_experts;
@@ -375,8 +369,6 @@ __global__ void __launch_bounds__(kProjThreads) k_project(ProjPlanArgs a) {
   pdl_wait();
   if (a.zero_best && blockIdx.x == 0)
     for (int i = tid; i < a.zero_n; i += kProjThreads) a.zero_best[i] = 0ull;
-  if (a.zero_cnt && blockIdx.x == 0)
-    for (int i = tid; i < a.zero_cnt_n; i += kProjThreads) a.zero_cnt[i] = 0;
   if (tid < 2) need[tid] = 0;
   __syncthreads();
   if (tid < kProjTileQ) {
@@ -611,10 +603,7 @@ __host__ __device__ inline MmaSmem mma_smem_layout(int l, int h, int nsplit) {
   return m;
 }
 
-// kPartial: no cluster; every split CTA stores its partial rows to a.qpart and the scan
-// that follows sums them (in split order, then the bias: the arithmetic of the cluster
-// reduction, so q is bit-identical).
-template <typename TK, bool kPartial>
+template <typename TK>
 __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   extern __shared__ __align__(256) unsigned char psm[];
   ALUT_TRACE(0);
@@ -653,8 +642,6 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   pdl_wait();
   if (a.zero_best && blockIdx.x == 0)
     for (int i = tid; i < a.zero_n; i += kProjThreads) a.zero_best[i] = 0ull;
-  if (a.zero_cnt && blockIdx.x == 0)
-    for (int i = tid; i < a.zero_cnt_n; i += kProjThreads) a.zero_cnt[i] = 0;
   if (tid < 2) need[tid] = 0;
   __syncthreads();
   if (tid < kProjTileQ) {
@@ -673,7 +660,7 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   cg::cluster_group cluster = cg::this_cluster();
   // Every CTA of the cluster must be running before any writes into its shared memory:
   // arrive now, wait just before the first remote store (the MMAs run in between).
-  if (!kPartial) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   bool cluster_ready = false;
   for (int nt = warp; nt < ntiles; nt += kProjThreads / 32) {
     float c[4] = {0.f, 0.f, 0.f, 0.f};
@@ -719,13 +706,6 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
         }
       }
     }
-    if (kPartial) {
-      const int col = nt * 8 + 2 * tq;
-      float* dst = a.qpart + (static_cast<size_t>(qt) * a.nsplit + sp) * kProjTileQ * L + col;
-      *reinterpret_cast<float2*>(dst + gq * L) = make_float2(c[0], c[1]);
-      *reinterpret_cast<float2*>(dst + (gq + 8) * L) = make_float2(c[2], c[3]);
-      continue;
-    }
     // Push the partial rows to their owners' receive buffers (slot = this rank).
     if (!cluster_ready) {
       asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
@@ -741,9 +721,8 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
       dst[1] = c[2 * half + 1];
     }
   }
-  ALUT_TRACE(5);
-  if (kPartial) return;
   if (!cluster_ready) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // warps without n-tiles
+  ALUT_TRACE(5);
   cluster.sync();  // every partial row has arrived at its owner; nothing remote is read after this
   ALUT_TRACE(6);
   // The owner of rows [r0, r1) sums the ranks' partials in rank order and finishes them.

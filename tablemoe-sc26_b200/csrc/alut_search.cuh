@@ -13,7 +13,6 @@
 // order independence keeps results deterministic.
 #pragma once
 
-#include "alut_combine.cuh"
 #include "alut_common.cuh"
 
 namespace alut {
@@ -33,6 +32,8 @@ struct SearchArgs {
 constexpr int kTmaBuffers = 2;
 constexpr uint32_t kWaitLimit = 1u << 20;  // bounded mbarrier wait (iterations of try_wait)
 constexpr int kBatch = 4;                   // slots scored together per pass over a row
+constexpr int kDecodeMaxPairs = 256;
+constexpr int kDecodeMaxTokens = 32;
 
 // ---- TMA / mbarrier primitives ---------------------------------------------------------
 
@@ -379,96 +380,24 @@ struct DecodeScanArgs {
   const uint8_t* reuse;
   int64_t reuse_stride;
   int* err;
-  // Queries: finished rows in s.qlow, or (qpart != nullptr) the projection's per-split
-  // partial rows qpart[(qtile * nsplit + split) * 16 + row][L], summed here in split order,
-  // then the bias, the rounding to the key dtype and the optional L2 normalisation: the
-  // arithmetic of the cluster reduction (finish_rows), so the queries are bit-identical.
-  const float* qpart;
-  int nsplit, normalize;
-  float eps;
-  const float* bias[2];
-  // Fused combine (k_search_decode<.., true>): per-token completion counters, cleared by the
-  // projection; the CTA whose scan completes a token combines that token's row.
-  int* tokcnt;
-  CombineArgs c;
 };
 
-// Distinct tables among token t's searched slots (s_table of the batch in shared memory).
-__device__ __forceinline__ int token_tables(const int* s_table, int t, int S) {
-  int n = 0;
-  for (int i = 0; i < S; ++i) {
-    const int ti = s_table[t * S + i];
-    if (ti < 0) continue;
-    bool first = true;
-    for (int j = 0; j < i; ++j) first &= (s_table[t * S + j] != ti);
-    n += first;
-  }
-  return n;
-}
-
-// Queries of slots pid[0, cnt) into qs[j * L + c], one warp per slot.
 template <typename TK>
-__device__ __forceinline__ void decode_queries(const DecodeScanArgs& d, const int* pid, int cnt, float* qs,
-                                               const float (*s_bias)[kMaxL]) {
-  const int L = d.s.l, S = d.s.s;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (!d.qpart) {
-    for (int i = threadIdx.x; i < cnt * L; i += kSearchThreads) {
-      const int j = i / L, c = i % L;
-      qs[i] = d.s.qlow[static_cast<int64_t>(pid[j] / S) * L + c];
-    }
-    return;
-  }
-  for (int j = warp; j < cnt; j += kSearchThreads / 32) {
-    const int tok = pid[j] / S;
-    const int qt = tok / kProjTileQ, r = tok % kProjTileQ;
-    const float* b = s_bias[d.is_vision[tok] ? 0 : 1];
-    const float* part = d.qpart + (static_cast<size_t>(qt) * d.nsplit * kProjTileQ + r) * L;
-    const size_t step = static_cast<size_t>(kProjTileQ) * L;
-    float ss = 0.f;
-    for (int c = lane; c < L; c += 32) {
-      float v = 0.f;
-      for (int k = 0; k < d.nsplit; ++k) v += __ldcg(part + k * step + c);
-      v = round_as<TK>(v + b[c]);
-      qs[j * L + c] = v;
-      ss = fmaf(v, v, ss);
-    }
-    if (d.normalize) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float n = round_as<TK>(sqrtf(ss));
-      const float eps = round_as<TK>(d.eps);
-      const float denom = fmaxf(n, eps);
-      const bool zero = n <= eps;
-      for (int c = lane; c < L; c += 32) qs[j * L + c] = zero ? 0.f : round_as<TK>(qs[j * L + c] / denom);
-    }
-  }
-}
-
-// Grid (slot, 128-centroid chunk). The first searched slot routed to a table leads: its CTAs
-// scan their chunk for every slot of that table. kFuse: each leader then counts the chunk
-// as done for each token among its slots, and the CTA that completes a token (all chunks of
-// all its tables) combines it; the CTA of a token's slot 0 combines tokens with no searched
-// slot. No CTA waits on another.
-template <typename TK, typename TV, bool kFuse>
 __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs d) {
   extern __shared__ __align__(128) unsigned char sm[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
   const SearchArgs& a = d.s;
-  const int L = a.l, S = a.s;
+  const int L = a.l;
   const int pitch = key_pitch(L, sizeof(TK));
   unsigned char* kbuf = sm + 128;
   float* qs = reinterpret_cast<float*>(sm + 128 + static_cast<size_t>(kSearchChunkK) * pitch);
   __shared__ int s_table[kDecodeMaxPairs];
-  __shared__ int s_pid[kDecodeMaxPairs];
-  __shared__ float s_bias[2][kMaxL];
   __shared__ float red_s[kSearchThreads / 32][kSearchGroup];
   __shared__ int red_k[kSearchThreads / 32][kSearchGroup];
-  __shared__ int s_cnt, s_abort, s_nfin;
-  __shared__ int s_fin[kDecodeMaxTokens];
-  __shared__ CombineSmem s_comb;
+  __shared__ int pid[kSearchGroup];
+  __shared__ int s_cnt, s_abort;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int pairs = d.q * S;
+  const int pairs = d.q * a.s;
   const int p = blockIdx.x;
   const int chunk = blockIdx.y;
   ALUT_TRACE(10);
@@ -476,18 +405,12 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
 
   // Table of every slot of the batch (-1: not searched or bad expert id).
   for (int i = tid; i < pairs; i += kSearchThreads) {
-    const int qq = i / S, ss = i % S;
+    const int qq = i / a.s, ss = i % a.s;
     const bool r = d.reuse ? (d.reuse[qq * d.reuse_stride + ss] != 0) : true;
     const int64_t e = d.sel[qq * d.sel_stride + ss];
     s_table[i] = (r && e >= 0 && e < d.num_experts) ? static_cast<int>(e) * 2 + (d.is_vision[qq] ? 0 : 1) : -1;
   }
   __syncthreads();
-  if (kFuse && chunk == 0 && p % S == 0 && token_tables(s_table, p / S, S) == 0) {
-    // A token with nothing to search: its row is still renormalised and written.
-    pdl_wait();
-    combine_token<TV, TV, true>(d.c, p / S, 0, d.c.h, true, s_comb);
-    return;
-  }
   const int table = s_table[p];
   if (table < 0) return;
   // Leader: the first searched slot routed to this table scans it for all of them.
@@ -496,21 +419,19 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
   if (__syncthreads_or(dup)) return;
   if (warp == 0) {
     int n = 0;
-    for (int base = p; base < pairs; base += 32) {
+    for (int base = p; base < pairs && n < kSearchGroup; base += 32) {
       const int i = base + lane;
       const bool m = i < pairs && s_table[i] == table;
       const unsigned bal = __ballot_sync(0xffffffffu, m);
-      if (m) s_pid[n + __popc(bal & ((1u << lane) - 1u))] = i;
+      const int pos = n + __popc(bal & ((1u << lane) - 1u));
+      if (m && pos < kSearchGroup) pid[pos] = i;
       n += __popc(bal);
     }
     if (lane == 0) {
-      s_cnt = n;
+      s_cnt = min(n, kSearchGroup);
       s_abort = 0;
-      s_nfin = 0;
     }
   }
-  if (d.qpart)
-    for (int i = tid; i < 2 * L; i += kSearchThreads) s_bias[i / L][i % L] = d.bias[i / L][i % L];
   const int rows = min(kSearchChunkK, a.k - chunk * kSearchChunkK);
   const uint32_t row_bytes = static_cast<uint32_t>(L) * sizeof(TK);
   if (tid == 0) {
@@ -525,63 +446,49 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
                     (static_cast<int64_t>(chunk) * kSearchChunkK + tid) * L;
     bulk_g2s(kbuf + static_cast<size_t>(tid) * pitch, src, row_bytes, &bar[0]);
   }
-  const int n = s_cnt;
+  const int cnt = s_cnt;
   ALUT_TRACE(11);
-  // The queries (and the cleared best buffer and counters) come from the projection kernel.
+  // The queries (and the cleared best buffer) come from the projection kernel.
   pdl_wait();
   ALUT_TRACE(12);
-  const TK* row = reinterpret_cast<const TK*>(kbuf + static_cast<size_t>(tid) * pitch);
-  const int cnt0 = min(kSearchGroup, n);
-  decode_queries<TK>(d, s_pid, cnt0, qs, s_bias);
+  for (int i = tid; i < cnt * L; i += kSearchThreads) {
+    const int j = i / L, c = i % L;
+    qs[i] = a.qlow[static_cast<int64_t>(pid[j] / a.s) * L + c];
+  }
   if (tid == 0 && !mbar_wait_bounded(&bar[0], 0)) {
     s_abort = 1;
     atomicOr(d.err, 4);
   }
   __syncthreads();
-  if (!s_abort) {
-    const bool ok = mbar_try_wait(&bar[0], 0);  // completed: acquire for this thread
-    const bool valid = ok && tid < rows;
-    ALUT_TRACE(13);
-    if (L == 64)
-      score_row_fixed<TK, 64>(row, valid, qs, cnt0, chunk * kSearchChunkK, red_s, red_k);
-    else if (L == 128)
-      score_row_fixed<TK, 128>(row, valid, qs, cnt0, chunk * kSearchChunkK, red_s, red_k);
-    else
-      score_row<TK, true>(row, valid, qs, L, cnt0, chunk * kSearchChunkK, red_s, red_k);
-    __syncthreads();
-    ALUT_TRACE(14);
-    fold_slots(cnt0, s_pid, a.idx_offset, a.best, red_s, red_k);
-    // More than kSearchGroup slots on one table (repeated experts): further groups.
-    for (int base = kSearchGroup; base < n; base += kSearchGroup) {
-      const int cnt = min(kSearchGroup, n - base);
-      __syncthreads();  // qs and the reduction arrays are free again
-      decode_queries<TK>(d, s_pid + base, cnt, qs, s_bias);
-      __syncthreads();
-      score_row<TK, true>(row, valid, qs, L, cnt, chunk * kSearchChunkK, red_s, red_k);
-      __syncthreads();
-      fold_slots(cnt, s_pid + base, a.idx_offset, a.best, red_s, red_k);
-    }
-  } else if (tid == 0) {
-    mbar_wait_bounded(&bar[0], 0);  // give the timed-out copy a bounded chance to land
+  if (s_abort) {
+    if (tid == 0) mbar_wait_bounded(&bar[0], 0);
+    return;
   }
+  ALUT_TRACE(13);
+  const bool ok = mbar_try_wait(&bar[0], 0);
+  const TK* row = reinterpret_cast<const TK*>(kbuf + static_cast<size_t>(tid) * pitch);
+#ifdef ALUT_PHASE_TRACE
+  {
+    const long long c0 = clock64();
+    if (L == 64) score_row_fixed<TK, 64>(row, ok && tid < rows, qs, cnt, chunk * kSearchChunkK, red_s, red_k);
+    const long long c1 = clock64();
+    ALUT_TRACE_VAL(30, c1 - c0);
+    ALUT_TRACE_VAL(31, cnt);
+    ALUT_TRACE_VAL(32, rows);
+  }
+  __syncthreads();
+  ALUT_TRACE(16);
+#endif
+  if (L == 64)
+    score_row_fixed<TK, 64>(row, ok && tid < rows, qs, cnt, chunk * kSearchChunkK, red_s, red_k);
+  else if (L == 128)
+    score_row_fixed<TK, 128>(row, ok && tid < rows, qs, cnt, chunk * kSearchChunkK, red_s, red_k);
+  else
+    score_row<TK, true>(row, ok && tid < rows, qs, L, cnt, chunk * kSearchChunkK, red_s, red_k);
+  __syncthreads();
+  ALUT_TRACE(14);
+  fold_slots(cnt, pid, a.idx_offset, a.best, red_s, red_k);
   ALUT_TRACE(15);
-  if (!kFuse) return;
-  // This chunk is done for every token among the slots: count it once per token, after
-  // publishing this CTA's folds (each folding thread fences its atomics).
-  __threadfence();
-  __syncthreads();
-  const int nchunks = gridDim.y;
-  for (int i = tid; i < n; i += kSearchThreads) {
-    const int tok = s_pid[i] / S;
-    if (i > 0 && s_pid[i - 1] / S == tok) continue;
-    const int need = token_tables(s_table, tok, S) * nchunks;
-    if (atomicAdd(d.tokcnt + tok, 1) == need - 1) s_fin[atomicAdd(&s_nfin, 1)] = tok;
-  }
-  __syncthreads();
-  const int nfin = s_nfin;
-  if (nfin == 0) return;
-  __threadfence();  // the other CTAs' folds, published before their counts, are visible
-  for (int f = 0; f < nfin; ++f) combine_token<TV, TV, true>(d.c, s_fin[f], 0, d.c.h, true, s_comb);
 }
 
 // ---- packed best -> (hit, idx) (search.py:597-602 / :689-697) -------------------------------
