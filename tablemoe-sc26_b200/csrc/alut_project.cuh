@@ -663,7 +663,9 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   bool cluster_ready = false;
   for (int nt = warp; nt < ntiles; nt += kProjThreads / 32) {
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    // One accumulator per basis part: three independent MMA chains, added (hi + mid) + lo
+    // at the end.
+    float cp[3][4] = {};
     for (int kb = k_begin; kb < k_end; kb += kMmaKBlock) {
       const int kn = min(kMmaKBlock, k_end - kb);
       uint32_t xa[kMmaKBlock][4];
@@ -700,12 +702,15 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
                 b0 = *reinterpret_cast<const uint32_t*>(bg);
                 b1 = *reinterpret_cast<const uint32_t*>(bg + 8);
               }
-              mma_bf16_16816(c, am, b0, b1);
+              mma_bf16_16816(cp[part], am, b0, b1);
             }
           }
         }
       }
     }
+    float c[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c[i] = (cp[0][i] + cp[1][i]) + cp[2][i];
     // Push the partial rows to their owners' receive buffers (slot = this rank).
     if (!cluster_ready) {
       asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
