@@ -265,11 +265,16 @@ int alut_gather_rows_sharded(int32_t n, const uint8_t* hit, const int64_t* idx, 
  * CUDA allocator, a serving loop that forbids cudaMalloc after start-up because it can
  * synchronise the device). It has no counterpart in the reference. Its scratch is a
  * fixed 2 MiB array inside this library (held by every GPU that loads the library until
- * the process exits); batches whose scratch would exceed it (alut_workspace_size() >
- * ALUT_NOALLOC_SCRATCH_BYTES) are rejected with ALUT_ERANGE. The first call on a device
- * looks up the array's device address (make it before any stream capture). All calls on
- * a device share the array: calls that may overlap on the GPU (different streams without
- * ordering between them) race and give wrong results. It calls no cudaMalloc/cudaFree. */
+ * the process exits). A batch is rejected with ALUT_ERANGE when the scratch of the
+ * CUDA-core scans (workspace layout without the tensor-core part) exceeds
+ * ALUT_NOALLOC_SCRATCH_BYTES; a batch that would take the tensor-core scan uses it only
+ * when that larger layout also fits, and otherwise runs the CUDA-core scan (same results).
+ * The first call on a device (and on each new CUDA context of it, e.g. after a
+ * cudaDeviceReset) looks up the array's device address: make it before any stream
+ * capture. All calls on a device share the array: calls that may overlap on the GPU
+ * (different streams without ordering between them) race and give wrong results. The
+ * error bits of the array are cleared at the start of every call (read them with
+ * alut_workspace_errors(NULL, ...)). It calls no cudaMalloc/cudaFree. */
 #define ALUT_NOALLOC_SCRATCH_BYTES (2u << 20)
 int alut_lookup_combine_noalloc(const alut_tables_t* tables, const alut_batch_t* batch,
                                 const alut_search_params_t* params, const float* weights,
@@ -278,6 +283,19 @@ int alut_lookup_combine_noalloc(const alut_tables_t* tables, const alut_batch_t*
                                 void* out, int64_t out_stride, int32_t out_dtype,
                                 uint8_t* out_hit, int64_t* out_idx, int64_t out_stride_hit,
                                 alut_stream_t stream);
+
+/* Device-side error bits of a workspace (or, with workspace NULL, of the no-allocation
+ * entry point's scratch). Kernels set them and never clear them, so they accumulate over
+ * every call that used the workspace until this function clears them (clear != 0). It
+ * waits for the stream (cudaStreamSynchronize), so it belongs in debug checks, not on the
+ * hot path. A set bit means some slot's result is wrong (a bad id leaves its slot a miss;
+ * a timed-out wait leaves its tile unscored); the reference raises IndexError for the
+ * first and has no counterpart of the others. */
+#define ALUT_ERR_BAD_EXPERT 1u  /* a searched slot's expert id is outside [0, num_experts) */
+#define ALUT_ERR_COPY_TIMEOUT 4u /* a key-chunk copy did not land within 1 s */
+#define ALUT_ERR_MMA_TIMEOUT 8u  /* a tensor-core pipeline wait ran out (1 s) */
+int alut_workspace_errors(void* workspace, size_t workspace_bytes, int32_t clear, uint32_t* bits,
+                          alut_stream_t stream);
 
 /* Profiling hook: when both events are set (cudaEvent_t handles), every following
  * centroid-scan launch made by this thread is bracketed by event records on its stream

@@ -20,6 +20,7 @@
 
 namespace alut {
 
+static void* noalloc_scratch_ptr(int* rc);
 static thread_local char g_err[512] = "no error";
 static thread_local cudaEvent_t g_prof_start = nullptr;
 static thread_local cudaEvent_t g_prof_stop = nullptr;
@@ -334,7 +335,6 @@ static int launch_plan(const ProjPlanArgs& a, int* tabs, cudaStream_t st) {
   const int64_t pairs = static_cast<int64_t>(a.q) * a.s;
   if (pairs > kPlanWideSlots) {
     cudaError_t e = cudaMemsetAsync(tabs, 0, sizeof(int) * ntab, st);
-    if (e == cudaSuccess) e = cudaMemsetAsync(a.meta + 1, 0, sizeof(int), st);
     if (e != cudaSuccess) return fail(ALUT_ECUDA, "plan: %s", cudaGetErrorString(e));
     const int grid = static_cast<int>(std::min<int64_t>((pairs + 255) / 256, static_cast<int64_t>(num_sms()) * 4));
     const size_t hs = sizeof(int) * ntab;
@@ -762,6 +762,31 @@ int alut_gather_rows_sharded(int32_t n, const uint8_t* hit, const int64_t* idx, 
   return check_launch("k_gather_sharded");
 }
 
+int alut_workspace_errors(void* workspace, size_t workspace_bytes, int32_t clear, uint32_t* bits,
+                          alut_stream_t stream) {
+  if (!bits) return fail(ALUT_EINVAL, "workspace_errors: bits is NULL");
+  if (!workspace) {  // the no-allocation entry point's scratch
+    int rc = ALUT_OK;
+    workspace = noalloc_scratch_ptr(&rc);
+    if (!workspace) return rc;
+    workspace_bytes = ALUT_NOALLOC_SCRATCH_BYTES;
+  }
+  if (workspace_bytes < 256) return fail(ALUT_EWORKSPACE, "workspace_errors: workspace too small");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // meta sits at offset 0 of every workspace layout; meta[1] is the error word.
+  int32_t* word = static_cast<int32_t*>(workspace) + 1;
+  uint32_t host = 0;
+  cudaError_t e = cudaMemcpyAsync(&host, word, sizeof(host), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && clear && host) {
+    e = cudaMemsetAsync(word, 0, sizeof(int32_t), st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  if (e != cudaSuccess) return fail(ALUT_ECUDA, "workspace_errors: %s", cudaGetErrorString(e));
+  *bits = host;
+  return ALUT_OK;
+}
+
 int alut_set_profile_events(void* start_event, void* stop_event) {
   if ((start_event == nullptr) != (stop_event == nullptr))
     return fail(ALUT_EINVAL, "profile events must be both set or both NULL");
@@ -1105,9 +1130,15 @@ int alut_merge_packed(int32_t world, int32_t q, int32_t s, const uint64_t* packe
 static __device__ __align__(256) unsigned char g_noalloc_scratch[ALUT_NOALLOC_SCRATCH_BYTES];
 
 namespace alut {
+// The array's address is resolved once per (device, CUDA context): a context created after a
+// cudaDeviceReset (or a caller's own driver-API context) loads the module again and gets a
+// fresh copy of the array, so the cached address is only reused within the same context.
 static void* noalloc_scratch_ptr(int* rc) {
-  static void* ptrs[64] = {nullptr};
+  struct Entry { void* ctx; void* ptr; };
+  static Entry cache[64] = {};
   static std::mutex mu;
+  using GetCtx = CUresult (*)(CUcontext*);
+  static GetCtx get_ctx = nullptr;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= 64) {
@@ -1115,17 +1146,29 @@ static void* noalloc_scratch_ptr(int* rc) {
     return nullptr;
   }
   std::lock_guard<std::mutex> lock(mu);
-  if (!ptrs[dev]) {
+  if (!get_ctx) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && fn)
+      get_ctx = reinterpret_cast<GetCtx>(fn);
+  }
+  // Before the runtime's first call on this thread there may be no current context yet;
+  // cudaGetSymbolAddress binds it, and the key is read again after it.
+  CUcontext ctx = nullptr;
+  if (get_ctx) get_ctx(&ctx);
+  if (!cache[dev].ptr || !ctx || cache[dev].ctx != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p) {
       *rc = fail(ALUT_ECUDA, "noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
       return nullptr;
     }
-    ptrs[dev] = p;
+    if (get_ctx) get_ctx(&ctx);
+    cache[dev] = Entry{ctx, p};
   }
   *rc = ALUT_OK;
-  return ptrs[dev];
+  return cache[dev].ptr;
 }
 }  // namespace alut
 

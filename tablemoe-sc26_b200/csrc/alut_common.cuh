@@ -24,6 +24,12 @@ constexpr int kMaxSlots = 64;            // top_k
 constexpr int kCombineThreads = 64;      // 8 elements per thread -> 512 per CTA
 constexpr int kProjSplitTarget = 296;    // 2 CTAs per SM over 148 SMs
 
+// Error bits of the workspace's meta[1] word (ALUT_ERR_* in alut.h). Kernels only set them
+// (atomicOr); they stay set until alut_workspace_errors clears them.
+constexpr int kErrBadExpert = 1;    // a searched slot's expert id is outside [0, num_experts)
+constexpr int kErrCopyTimeout = 4;  // a TMA / bulk copy did not land within the wait limit
+constexpr int kErrMmaTimeout = 8;   // a tensor-core pipeline wait ran out
+
 // ---- element conversion ---------------------------------------------------------
 
 template <typename T> __device__ __forceinline__ float to_f32(T v);

@@ -112,7 +112,6 @@ __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
   __shared__ int scan_scratch[kProjThreads];
   __shared__ int s_tot_c, s_tot_g;
 
-  if (tid == 0) a.meta[1] = 0;
   for (int t = tid; t < ntab; t += kProjThreads) counts[t] = 0;
   __syncthreads();
   for (int64_t p = tid; p < pairs; p += kProjThreads) {
@@ -122,7 +121,7 @@ __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
     if (!r) continue;
     const int64_t e = a.sel[qq * a.sel_stride + ss];
     if (e < 0 || e >= a.num_experts) {
-      atomicOr(&a.meta[1], 1);
+      atomicOr(&a.meta[1], kErrBadExpert);
       continue;
     }
     atomicAdd(&counts[static_cast<int>(e) * 2 + (a.is_vision[qq] ? 0 : 1)], 1);
@@ -168,7 +167,7 @@ __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
 // (2) k_plan_groups (one CTA): scans the counts into bucket offsets and the group list;
 // (3) k_plan_scatter: writes each searched slot id into its table's bucket (warp-aggregated
 //     atomics on the bucket cursors). The order inside a bucket does not matter.
-// `counts` must be zero before (1); meta[1] (error bits) likewise.
+// `counts` must be zero before (1).
 
 // Table of slot p, or -1 when the slot is not searched (reuse mask off) or its expert id is
 // out of range (then *bad is set).
@@ -203,7 +202,7 @@ __global__ void __launch_bounds__(256) k_plan_count(ProjPlanArgs a, int* counts)
     const unsigned same = __match_any_sync(0xffffffffu, t);
     if (t >= 0 && lane == __ffs(same) - 1) atomicAdd(&hist[t], __popc(same));
   }
-  if (bad) atomicOr(&a.meta[1], 1);
+  if (bad) atomicOr(&a.meta[1], kErrBadExpert);
   __syncthreads();
   for (int t = threadIdx.x; t < ntab; t += blockDim.x)
     if (hist[t]) atomicAdd(&counts[t], hist[t]);

@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
       s_issued = it;
       if (!ok && !*abort_flag) {
         *abort_flag = 1;
-        atomicOr(a.err, 8);
+        atomicOr(a.err, kErrMmaTimeout);
       }
     }
   } else if (warp == 8) {
@@ -316,7 +316,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
       }
       if (!ok && !*abort_flag) {
         *abort_flag = 1;
-        atomicOr(a.err, 8);
+        atomicOr(a.err, kErrMmaTimeout);
       }
     }
   } else if (warp < 4) {
@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(kPtThreads, 1) k_project_tc(const __grid_const
       if (__any_sync(0xffffffffu, !ok)) {
         if (lane == 0 && !*abort_flag) {
           *abort_flag = 1;
-          atomicOr(a.err, 8);
+          atomicOr(a.err, kErrMmaTimeout);
         }
         break;
       }

@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_tma(SearchArgs a, int
     }
     if (tid == 0 && !mbar_wait_bounded(&bar[b], parity)) {
       s_abort = 1;
-      atomicOr(err, 4);
+      atomicOr(err, kErrCopyTimeout);
     }
     __syncthreads();
     if (s_abort) break;
@@ -408,7 +408,10 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
     const int qq = i / a.s, ss = i % a.s;
     const bool r = d.reuse ? (d.reuse[qq * d.reuse_stride + ss] != 0) : true;
     const int64_t e = d.sel[qq * d.sel_stride + ss];
-    s_table[i] = (r && e >= 0 && e < d.num_experts) ? static_cast<int>(e) * 2 + (d.is_vision[qq] ? 0 : 1) : -1;
+    const bool in_range = e >= 0 && e < d.num_experts;
+    s_table[i] = (r && in_range) ? static_cast<int>(e) * 2 + (d.is_vision[qq] ? 0 : 1) : -1;
+    // One CTA reports searched slots with an out-of-range expert id (sticky error bit).
+    if (r && !in_range && blockIdx.x == 0 && blockIdx.y == 0) atomicOr(d.err, kErrBadExpert);
   }
   __syncthreads();
   const int table = s_table[p];
@@ -457,7 +460,7 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
   }
   if (tid == 0 && !mbar_wait_bounded(&bar[0], 0)) {
     s_abort = 1;
-    atomicOr(d.err, 4);
+    atomicOr(d.err, kErrCopyTimeout);
   }
   __syncthreads();
   if (s_abort) {

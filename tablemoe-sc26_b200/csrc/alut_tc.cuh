@@ -21,12 +21,14 @@
 //
 // Pipeline (one CTA per SM, persistent over a contiguous range of (group, chunk) tiles so
 // that a group's query tile is loaded once and its chunks stream in order):
-//   warp 4 (producer): query tile -> A[2], key chunk -> stage ring (mbarrier full/empty);
-//   warp 5 (MMA): allocates 256 TMEM columns, issues L/16 MMAs per tile into one of two
-//                 accumulators, commits to the stage's `empty`, the accumulator's `full`
-//                 and, at a group's last tile, the query buffer's `empty` barrier;
-//   warps 0-3 (epilogue): thread r reads TMEM lane r (slot r of the group), 128 columns,
-//                 releases the accumulator, filters, rescores at the group's end.
+//   warp 8 (producer): query tile -> A[2], key chunk -> stage ring (mbarrier full/empty);
+//   warp 9 (MMA): allocates all 512 TMEM columns, issues L/16 MMAs per tile into one of
+//                 four 128-column fp32 accumulators, commits to the stage's `empty`, the
+//                 accumulator's `full` and, at a group's last tile, the query buffer's
+//                 `empty` barrier;
+//   warps 0-7 (epilogue): warp w reads TMEM lane quarter w % 4 (slots 32 (w % 4)..) over
+//                 centroid columns 64 (w / 4).. of the tile, releases the accumulator,
+//                 filters candidates and rescores them at the group's end.
 // Every wait is bounded in time; on expiry the CTA records an error bit, stops all roles,
 // drains what it has in flight (bounded), frees TMEM and returns.
 #pragma once
@@ -483,7 +485,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       s_groups_issued = gi + 1;
       if (!ok && !*abort_flag) {
         *abort_flag = 1;
-        atomicOr(a.err, 8);
+        atomicOr(a.err, kErrMmaTimeout);
       }
     }
   } else if (warp == kTcMmaWarp) {
@@ -544,7 +546,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       }
       if (!ok && !*abort_flag) {
         *abort_flag = 1;
-        atomicOr(a.err, 8);
+        atomicOr(a.err, kErrMmaTimeout);
       }
     }
   } else {
@@ -587,7 +589,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       if (__any_sync(0xffffffffu, !ok)) {
         if (lane == 0 && !*abort_flag) {
           *abort_flag = 1;
-          atomicOr(a.err, 8);
+          atomicOr(a.err, kErrMmaTimeout);
         }
         break;
       }

@@ -24,6 +24,7 @@ KEYS_NORMALISED, KEYS_RAW = 0, 1
 RENORM_NONE, RENORM_TO_ONE, RENORM_TO_ROWSUM = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 2 << 20  # ALUT_NOALLOC_SCRATCH_BYTES
 PEER_HANDLE_BYTES = 64  # ALUT_PEER_HANDLE_BYTES
+ERR_BAD_EXPERT, ERR_COPY_TIMEOUT, ERR_MMA_TIMEOUT = 1, 4, 8  # ALUT_ERR_* device error bits
 
 _DTYPE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
@@ -90,6 +91,7 @@ SIGNATURES = {
     "alut_peer_close": (ctypes.c_int, [_P, ctypes.c_uint64]),
     "alut_gather_rows_sharded": (ctypes.c_int, [_I32, _P, _P, _P, _I32, _P, _P, _P, _I64, _I32, _I32, _P, _I64,
                                                 _P]),
+    "alut_workspace_errors": (ctypes.c_int, [_P, _SZ, _I32, ctypes.POINTER(ctypes.c_uint32), _P]),
     "alut_set_profile_events": (ctypes.c_int, [_P, _P]),
     "alut_last_error": (ctypes.c_char_p, []),
     "alut_version": (ctypes.c_int, []),
@@ -129,6 +131,24 @@ def check(rc: int, what: str) -> None:
     if rc in (ALUT_EINVAL, ALUT_EDTYPE, ALUT_ESHAPE, ALUT_ERANGE):
         raise ValueError(f"{what}: {msg} (status {rc})")
     raise RuntimeError(f"{what}: {msg} (status {rc})")
+
+
+def device_errors(workspace, nbytes, device, clear=True) -> int:
+    """Error bits the kernels left in a workspace (workspace None: the no-allocation
+    scratch); waits for the current stream."""
+    bits = ctypes.c_uint32(0)
+    check(load().alut_workspace_errors(workspace, nbytes, int(clear), ctypes.byref(bits), stream_ptr(device)),
+          "alut_workspace_errors")
+    return int(bits.value)
+
+
+def raise_device_errors(bits: int, what: str) -> None:
+    """Map device error bits to the exceptions the reference raises (IndexError for an
+    expert id outside the table, as its tensor indexing does) or RuntimeError."""
+    if bits & ERR_BAD_EXPERT:
+        raise IndexError(f"{what}: a searched slot's expert id is outside [0, num_experts)")
+    if bits:
+        raise RuntimeError(f"{what}: a device wait timed out (error bits {bits:#x}); results are incomplete")
 
 
 def dtype_code(dt: torch.dtype) -> int:

@@ -39,6 +39,10 @@ def _defaults() -> dict:
         "OFFLINE_COSINE_THRESHOLD_TEXT": 0.7,
         "OFFLINE_DOT_THRESHOLD": 0.0,
         "OFFLINE_COSINE_EPS": 1e-6,
+        # Not in the reference: read the kernels' device error bits after every search
+        # (synchronises the stream; raises IndexError for out-of-range expert ids, as the
+        # reference's indexing does, and RuntimeError for timed-out device waits).
+        "ALUT_CHECK_ERRORS": os.getenv("TABLEMOE_ALUT_CHECK_ERRORS", "0") == "1",
     }
 
 

@@ -95,6 +95,16 @@ class VectorSearchEngine:
             self._alut_ws_shape = (cq, cs)
         return self._alut_ws
 
+    def device_errors(self, clear=True):
+        """Device error bits (ALUT_ERR_*) accumulated in this engine's workspace since the last
+        clear; synchronises the current stream."""
+        if self._alut_ws is None:
+            return 0
+        return _alut.device_errors(self._alut_ws.data_ptr(), self._alut_ws.numel(), self.device, clear)
+
+    def check_device_errors(self, what="ALUT"):
+        _alut.raise_device_errors(self.device_errors(clear=True), what)
+
     def _ensure_workspace(self, batch_size, top_k):
         if batch_size > self.workspace_capacity or self.workspace.get("top_k") != top_k:
             cap = max(batch_size, 128)
@@ -139,6 +149,8 @@ class VectorSearchEngine:
                                    out_hit.stride(0), ws.data_ptr(), ws.numel(),
                                    _alut.stream_ptr(self.device))
         _alut.check(rc, "alut_search")
+        if CacheConfig.ALUT_CHECK_ERRORS:
+            self.check_device_errors("alut_search")
 
     def _new_outputs(self, selected_experts):
         bs, top_k = selected_experts.shape
@@ -277,14 +289,16 @@ class VectorSearchEngine:
     # ---- fused lookup (search + gather + weighted accumulate) --------------------------
     def lookup_combine(self, hidden_states, selected_experts, is_vision_mask, reuse_mask, routing_weights,
                        *, compute_mask=None, out=None, variant="prefill_dot", renorm="to_one",
-                       return_hits=False):
+                       return_hits=False, hit_out=None, idx_out=None):
         """Search every reuse slot, then out[t] (+)= sum over hits of w~[t,s] * value row.
 
         ``variant`` picks the search semantics of one of the methods above ("prefill",
         "prefill_dot", "decode", "decode_dot"); ``renorm`` is "none", "to_one" (Qwen3-VL
         combine, cached_layers.py:463-465) or "to_rowsum" (DeepSeek-VL2,
         deepseek_layers.py:715-727). ``out`` (accumulated into when given) defaults to a
-        new [bs, H] tensor of the value dtype.
+        new [bs, H] tensor of the value dtype. ``hit_out`` / ``idx_out`` ([bs, top_k] bool /
+        int64, unit inner stride, shared strides) receive the hits and indices in place;
+        ``return_hits`` allocates them instead.
         """
         rules = {
             "prefill": (_alut.KEYS_NORMALISED, True, True, CacheConfig.OFFLINE_COSINE_THRESHOLD_VISION,
@@ -302,6 +316,12 @@ class VectorSearchEngine:
         if out is None:
             out = torch.empty((bs, values.shape[-1]), dtype=values.dtype, device=self.device)
         hit, idx = self._new_outputs(selected_experts) if return_hits else (None, None)
+        if hit_out is not None or idx_out is not None:
+            if hit_out is None or idx_out is None or hit_out.shape != selected_experts.shape or \
+                    idx_out.shape != selected_experts.shape or hit_out.stride() != idx_out.stride() or \
+                    hit_out.stride(-1) != 1 or hit_out.dtype != torch.bool or idx_out.dtype != torch.int64:
+                raise ValueError("hit_out / idx_out: [bs, top_k] bool and int64 with shared unit-inner strides")
+            hit, idx = hit_out, idx_out
         if bs and top_k:
             w = routing_weights if routing_weights.dtype == torch.float32 else routing_weights.float()
             w = w if w.stride(-1) == 1 else w.contiguous()
@@ -322,9 +342,12 @@ class VectorSearchEngine:
             rc = self._lib.alut_lookup_combine(
                 tables, batch, params, w.data_ptr(), w.stride(0), _alut.ptr(comp),
                 0 if comp is None else comp.stride(0), rn, int(accumulate), out.data_ptr(), out.stride(0),
-                _alut.dtype_code(out.dtype), _alut.ptr(hit), _alut.ptr(idx), top_k, ws.data_ptr(),
+                _alut.dtype_code(out.dtype), _alut.ptr(hit), _alut.ptr(idx), top_k if hit is None else hit.stride(0),
+                ws.data_ptr(),
                 ws.numel(), _alut.stream_ptr(self.device))
             _alut.check(rc, "alut_lookup_combine")
+            if CacheConfig.ALUT_CHECK_ERRORS:
+                self.check_device_errors("alut_lookup_combine")
         elif not accumulate:
             out.zero_()
         return (out, hit, idx) if return_hits else out

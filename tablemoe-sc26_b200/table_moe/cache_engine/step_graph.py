@@ -44,7 +44,10 @@ def _view(arena: torch.Tensor, off: int, shape, dtype):
 
 class LookupStepGraph:
     def __init__(self, engines, q, s, *, x_dtype=torch.bfloat16, variant="decode", renorm="to_one",
-                 accumulate=True):
+                 accumulate=True, keep_hits=False):
+        """``keep_hits``: every layer's lookup also writes its hits and centroid indices into
+        device tensors (``self.hits[i]``, ``self.idx[i]``, [q, s]) that stay out of the
+        host copies, so that a replay can be checked slot by slot."""
         if not engines:
             raise ValueError("need at least one engine")
         self.engines = list(engines)
@@ -78,6 +81,10 @@ class LookupStepGraph:
 
         self.layers = views(self.in_dev, self.out_dev)
         self.host_layers = views(self.in_host, self.out_host)
+        self.hits = [torch.zeros(q, s, dtype=torch.bool, device=self.device) for _ in self.engines] \
+            if keep_hits else None
+        self.idx = [torch.zeros(q, s, dtype=torch.int64, device=self.device) for _ in self.engines] \
+            if keep_hits else None
         self.graph = None
         self.with_copies = False
         self._events = None
@@ -97,7 +104,9 @@ class LookupStepGraph:
                 _alut.check(lib.alut_set_profile_events(st.cuda_event, sp.cuda_event), "profile events")
             out = eng.lookup_combine(b.x, b.sel, b.is_vision, b.reuse, b.weights, compute_mask=b.compute,
                                      out=b.out if self.accumulate else None, variant=self.variant,
-                                     renorm=self.renorm)
+                                     renorm=self.renorm,
+                                     hit_out=None if self.hits is None else self.hits[i],
+                                     idx_out=None if self.idx is None else self.idx[i])
             if not self.accumulate:
                 b.out.copy_(out)
 
@@ -138,6 +147,11 @@ class LookupStepGraph:
         if self.graph is None:
             raise RuntimeError("capture() first")
         self.graph.replay()
+
+    def check_errors(self):
+        """Raise if any layer's kernels left device error bits (synchronises)."""
+        for i, eng in enumerate(self.engines):
+            eng.check_device_errors(f"layer {i}")
 
     def scan_times_ms(self):
         """Per-layer centroid-scan durations of the last replay (needs profile events)."""

@@ -19,12 +19,13 @@ from pathlib import Path
 import numpy as np
 
 import oracle.oracle as orc
+import oracle.parity_rules as rules
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
-IDX_REL_TOL = 1e-5
-COMBINE_RTOL = 1e-2
-ULP = {"float32": 2.0 ** -23, "bfloat16": 2.0 ** -8, "float16": 2.0 ** -11}
+IDX_REL_TOL = rules.IDX_REL_TOL
+COMBINE_RTOL = rules.COMBINE_RTOL
+ULP = rules.ULP
 
 
 def golden_names():
@@ -81,45 +82,16 @@ def case_inputs(meta, d):
 def check_search(got_hit, got_idx, ref_hit, ref_idx, q_low, keys, sel, is_vision, thr, dtype,
                  what=""):
     """Assert the index / hit parity rules; returns the number of exempted slots."""
-    got_hit = np.asarray(got_hit).astype(bool)
-    ref_hit = np.asarray(ref_hit).astype(bool)
-    got_idx = np.asarray(got_idx)
-    ref_idx = np.asarray(ref_idx)
-    is_vision = np.asarray(is_vision).astype(bool)
-    ulp = ULP[dtype]
-    exempt = 0
-    bad = []
-    for t, s in zip(*np.nonzero((got_hit != ref_hit) | (got_hit & (got_idx != ref_idx)))):
-        s_ref = orc.score(q_low, keys, sel, is_vision, t, s, int(ref_idx[t, s]))
-        th = thr[0] if is_vision[t] else thr[1]
-        if got_hit[t, s] != ref_hit[t, s]:
-            # Only the hit differs: the best score must sit on the threshold.
-            best = s_ref if ref_hit[t, s] else orc.score(q_low, keys, sel, is_vision, t, s, int(got_idx[t, s]))
-            tol = max(IDX_REL_TOL, 2 * ulp) * max(abs(th), abs(best), 1e-30)
-            if abs(best - th) <= tol:
-                exempt += 1
-                continue
-            bad.append((t, s, "hit", bool(got_hit[t, s]), bool(ref_hit[t, s]), best, th))
-            continue
-        s_got = orc.score(q_low, keys, sel, is_vision, t, s, int(got_idx[t, s]))
-        tol = (IDX_REL_TOL if dtype == "float32" else 2 * ulp) * max(abs(s_ref), abs(s_got), 1e-30)
-        if abs(s_ref - s_got) <= tol:
-            exempt += 1
-            continue
-        bad.append((t, s, "idx", int(got_idx[t, s]), int(ref_idx[t, s]), s_got, s_ref))
+    bad, exempt = rules.search_mismatches(got_hit, got_idx, ref_hit, ref_idx, q_low, keys, sel, is_vision, thr,
+                                          dtype)
     assert not bad, f"{what}: {len(bad)} slots break the parity rule, first: {bad[:5]}"
-    # Misses and non-searched slots carry index 0 (the reference's pre-zeroed outputs).
-    assert np.all(got_idx[~got_hit] == 0), f"{what}: a miss carries a nonzero index"
     return exempt
 
 
 def check_combined(got, ref, what=""):
-    got = np.asarray(got, np.float32)
-    ref = np.asarray(ref, np.float32)
-    scale = float(np.max(np.abs(ref))) if ref.size else 0.0
-    err = np.abs(got - ref)
-    tol = COMBINE_RTOL * np.abs(ref) + COMBINE_RTOL * scale + 1e-12
-    assert np.all(err <= tol), f"{what}: combine max err {err.max()} (scale {scale})"
+    n, err = rules.combined_mismatches(got, ref)
+    scale = float(np.max(np.abs(np.asarray(ref, np.float32)))) if np.size(ref) else 0.0
+    assert n == 0, f"{what}: combine max err {err} (scale {scale})"
 
 
 def check_online(got_hit, got_idx, got_slot, ref_hit, ref_idx, ref_slot, scores, what=""):

@@ -94,3 +94,24 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_alut, "_lib", None)
     with pytest.raises(ImportError):
         _alut.load()
+
+
+def _integration_stub_structs():
+    """Run the struct definitions of the ctypes stub documented for maintainers (the python
+    block of INTEGRATION.md) without its library load or calls."""
+    text = (Path(__file__).resolve().parents[1] / "INTEGRATION.md").read_text()
+    block = re.search(r"```python\n(.*?)```", text, re.S).group(1)
+    defs = block[:block.index("lib.alut_search")].replace('lib = ctypes.CDLL("libalut.so")', "")
+    ns = {}
+    exec(defs, ns)
+    return ns
+
+
+@pytest.mark.parametrize("stub,ours", [("alut_tables_t", "Tables"), ("alut_batch_t", "Batch"),
+                                       ("alut_search_params_t", "SearchParams")])
+def test_integration_stub_matches_the_binding(stub, ours):
+    """The documented stub has the binding's size and field offsets (a short struct would
+    make the library read past its end)."""
+    a, b = _integration_stub_structs()[stub], getattr(_alut, ours)
+    assert ctypes.sizeof(a) == ctypes.sizeof(b)
+    assert [(n, getattr(a, n).offset) for n, _ in a._fields_] == [(n, getattr(b, n).offset) for n, _ in b._fields_]

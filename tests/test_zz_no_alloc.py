@@ -44,10 +44,11 @@ def manager():
 
 
 def _run(lib, mgr, c, noalloc):
-    tables = mgr.alut_tables()
+    Q, S = c["sel"].shape
+    # Batches of >= 512 slots take the tensor-core scan when the key form is prepared.
+    tables = mgr.prepare_tensor_core(_alut.KEYS_RAW) if Q * S >= 512 else mgr.alut_tables()
     batch = _alut.make_batch(c["x"], c["sel"], c["vis"], c["reuse"])
     params = _alut.make_params(_alut.KEYS_RAW, False, False, 0.0, 0.0, 1e-6)
-    Q, S = c["sel"].shape
     out = torch.full((Q, mgr.hidden_dim), 7.0, dtype=torch.bfloat16, device=DEV)
     hit = torch.zeros(Q, S, dtype=torch.bool, device=DEV)
     idx = torch.zeros(Q, S, dtype=torch.long, device=DEV)
@@ -64,10 +65,13 @@ def _run(lib, mgr, c, noalloc):
     return out, hit, idx
 
 
-def test_noalloc_matches_workspace_entry_on_consecutive_calls(manager):
+@pytest.mark.parametrize("Q,S", [(16, 8), (64, 4), (256, 4)])
+def test_noalloc_matches_workspace_entry_on_consecutive_calls(manager, Q, S):
+    """(16, 8): decode chain; (64, 4): planned CUDA-core scan; (256, 4): 1024 searched-or-not
+    slots on tables with the tensor-core key form (tensor-core scan when its layout fits)."""
     lib = _alut.load()
     for seed in (1, 2):  # two calls in a row, different batches, the shared scratch reused
-        c = _case(seed)
+        c = _case(seed, Q=Q, S=S)
         ref_out, ref_hit, ref_idx = _run(lib, manager, c, noalloc=False)
         out, hit, idx = _run(lib, manager, c, noalloc=True)
         assert torch.equal(hit, ref_hit) and torch.equal(idx, ref_idx)
