@@ -439,9 +439,12 @@ static int launch_combine(int vd, int od, bool vec, const CombineArgs& a, dim3 g
 }
 
 // Projection + plan + centroid scan into the packed best buffer `best`.
+// prefetch_values: the value table when a combine follows (the decode scan then asks L2
+// for the rows of the running best candidates); NULL otherwise.
 static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_search_params_t* p,
                       const void* keys, const void* q_low_in, uint32_t idx_offset,
-                      uint64_t* best, void* workspace, size_t ws_bytes, cudaStream_t st) {
+                      uint64_t* best, void* workspace, size_t ws_bytes, cudaStream_t st,
+                      const void* prefetch_values = nullptr) {
   const Workspace w = workspace_layout(b->q, b->s, t->l, 2 * t->num_experts);
   if (!workspace) return fail(ALUT_EWORKSPACE, "workspace is NULL");
   if (ws_bytes < w.total)
@@ -511,6 +514,19 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     d.reuse = b->reuse;
     d.reuse_stride = b->reuse_stride;
     d.err = a.meta + 1;
+    {
+      const int vsz = dtype_size(t->value_dtype);
+      const int64_t rb = static_cast<int64_t>(t->h) * vsz;
+      if (prefetch_values && aligned16(prefetch_values) && rb % 16 == 0 && rb < (1 << 20) &&
+          (t->value_stride[0] * vsz) % 16 == 0 && (t->value_stride[1] * vsz) % 16 == 0 &&
+          (t->value_stride[2] * vsz) % 16 == 0) {
+        d.values = static_cast<const unsigned char*>(prefetch_values);
+        d.vs_e = t->value_stride[0] * vsz;
+        d.vs_m = t->value_stride[1] * vsz;
+        d.vs_k = t->value_stride[2] * vsz;
+        d.row_bytes = static_cast<uint32_t>(rb);
+      }
+    }
     rc = launch_search_decode(t->key_dtype, d, dim3(pairs, d.s.nchunks), search_decode_smem_bytes(t->l, esz), st);
     if (rc) return rc;
     if (g_prof_start && g_prof_stop && record_profile(g_prof_stop, st)) return ALUT_ECUDA;
@@ -1048,7 +1064,7 @@ int alut_lookup_combine(const alut_tables_t* tables, const alut_batch_t* batch,
   if (!workspace || workspace_bytes < w.total)
     return fail(ALUT_EWORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, w.total);
   uint64_t* best = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + w.best);
-  rc = run_search(tables, batch, params, keys, nullptr, 0u, best, workspace, workspace_bytes, st);
+  rc = run_search(tables, batch, params, keys, nullptr, 0u, best, workspace, workspace_bytes, st, tables->values);
   if (rc) return rc;
   CombineArgs c{};
   fill_value_strides(tables, c);

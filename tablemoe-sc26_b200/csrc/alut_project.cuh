@@ -617,7 +617,6 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   const MmaSmem lay = mma_smem_layout(L, H, a.nsplit);
   float* recv = reinterpret_cast<float*>(psm + lay.recv);
   __shared__ int mod[kProjTileQ];
-  __shared__ int need[2];
   __shared__ float s_bias[2][kMaxL];
   const int ksteps = H / 16;
   const int k_begin = static_cast<int>(static_cast<int64_t>(sp) * ksteps / a.nsplit);
@@ -639,22 +638,39 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   }
   cp_async_commit();
   pdl_wait();
-  if (a.zero_best && blockIdx.x == 0)
-    for (int i = tid; i < a.zero_n; i += kProjThreads) a.zero_best[i] = 0ull;
-  if (tid < 2) need[tid] = 0;
-  __syncthreads();
-  if (tid < kProjTileQ) {
-    const int m = tid < nq ? (a.is_vision[q0 + tid] ? 0 : 1) : 1;
-    mod[tid] = m;
-    if (tid < nq) need[m] = 1;
-  }
+  // This call's inputs, requested together: the first k-block of this thread's x fragments
+  // and the modality of every row of the tile (each warp derives what it needs from the
+  // latter with shuffles and ballots, so no block barrier sits between the two loads).
   const bool row0_ok = gq < nq, row1_ok = gq + 8 < nq;
   const __nv_bfloat16* xr0 = static_cast<const __nv_bfloat16*>(a.x) + static_cast<int64_t>(q0 + (row0_ok ? gq : 0)) * a.x_stride;
   const __nv_bfloat16* xr1 = static_cast<const __nv_bfloat16*>(a.x) + static_cast<int64_t>(q0 + (row1_ok ? gq + 8 : 0)) * a.x_stride;
+  uint32_t xa[kMmaKBlock][4];
+  auto load_x = [&](int kb) {
+    const int kn = min(kMmaKBlock, k_end - kb);
+#pragma unroll
+    for (int s = 0; s < kMmaKBlock; ++s) {
+      if (s < kn) {
+        const int k0 = (kb + s) * 16 + 2 * tq;
+        xa[s][0] = row0_ok ? *reinterpret_cast<const uint32_t*>(xr0 + k0) : 0u;
+        xa[s][1] = row1_ok ? *reinterpret_cast<const uint32_t*>(xr1 + k0) : 0u;
+        xa[s][2] = row0_ok ? *reinterpret_cast<const uint32_t*>(xr0 + k0 + 8) : 0u;
+        xa[s][3] = row1_ok ? *reinterpret_cast<const uint32_t*>(xr1 + k0 + 8) : 0u;
+      }
+    }
+  };
+  int x_block = k_begin;  // the k-block whose fragments xa holds
+  if (warp < ntiles && k_begin < k_end) load_x(k_begin);
+  const bool lane_vis = lane < nq && a.is_vision[q0 + lane] != 0;
+  const unsigned vis_bits = __ballot_sync(0xffffffffu, lane_vis);
+  const unsigned rows_bits = nq >= 32 ? 0xffffffffu : ((1u << nq) - 1u);
+  const bool need_m[2] = {vis_bits != 0u, (rows_bits & ~vis_bits) != 0u};
+  const int m_r0 = (vis_bits >> gq) & 1u ? 0 : 1, m_r1 = (vis_bits >> (gq + 8)) & 1u ? 0 : 1;
+  if (warp == 0 && lane < kProjTileQ) mod[lane] = lane_vis ? 0 : 1;  // for finish_rows
+  if (a.zero_best && blockIdx.x == 0)
+    for (int i = tid; i < a.zero_n; i += kProjThreads) a.zero_best[i] = 0ull;
   cp_async_wait<0>();
   __syncthreads();
   ALUT_TRACE(1);
-  const int m_r0 = mod[gq], m_r1 = mod[gq + 8];
   const int rows_per = (kProjTileQ + a.nsplit - 1) / a.nsplit;
   cg::cluster_group cluster = cg::this_cluster();
   // Every CTA of the cluster must be running before any writes into its shared memory:
@@ -667,20 +683,13 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
     float cp[3][4] = {};
     for (int kb = k_begin; kb < k_end; kb += kMmaKBlock) {
       const int kn = min(kMmaKBlock, k_end - kb);
-      uint32_t xa[kMmaKBlock][4];
-#pragma unroll
-      for (int s = 0; s < kMmaKBlock; ++s) {
-        if (s < kn) {
-          const int k0 = (kb + s) * 16 + 2 * tq;
-          xa[s][0] = row0_ok ? *reinterpret_cast<const uint32_t*>(xr0 + k0) : 0u;
-          xa[s][1] = row1_ok ? *reinterpret_cast<const uint32_t*>(xr1 + k0) : 0u;
-          xa[s][2] = row0_ok ? *reinterpret_cast<const uint32_t*>(xr0 + k0 + 8) : 0u;
-          xa[s][3] = row1_ok ? *reinterpret_cast<const uint32_t*>(xr1 + k0 + 8) : 0u;
-        }
+      if (kb != x_block) {
+        load_x(kb);
+        x_block = kb;
       }
 #pragma unroll
       for (int m = 0; m < 2; ++m) {
-        if (!need[m]) continue;
+        if (!need_m[m]) continue;
         // Rows of the other modality are zeroed in A, so the two passes add exactly.
         const uint32_t keep0 = (m_r0 == m) ? 0xffffffffu : 0u, keep1 = (m_r1 == m) ? 0xffffffffu : 0u;
 #pragma unroll

@@ -380,7 +380,17 @@ struct DecodeScanArgs {
   const uint8_t* reuse;
   int64_t reuse_stride;
   int* err;
+  // Optional (lookup + combine): value rows of the tables, in bytes. A CTA whose chunk
+  // candidate becomes a slot's best so far asks L2 to fetch that centroid's value row, so
+  // the combine that follows reads the winners from L2 instead of HBM.
+  const unsigned char* values;
+  int64_t vs_e, vs_m, vs_k;
+  uint32_t row_bytes;
 };
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 template <typename TK>
 __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs d) {
@@ -470,18 +480,6 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
   ALUT_TRACE(13);
   const bool ok = mbar_try_wait(&bar[0], 0);
   const TK* row = reinterpret_cast<const TK*>(kbuf + static_cast<size_t>(tid) * pitch);
-#ifdef ALUT_PHASE_TRACE
-  {
-    const long long c0 = clock64();
-    if (L == 64) score_row_fixed<TK, 64>(row, ok && tid < rows, qs, cnt, chunk * kSearchChunkK, red_s, red_k);
-    const long long c1 = clock64();
-    ALUT_TRACE_VAL(30, c1 - c0);
-    ALUT_TRACE_VAL(31, cnt);
-    ALUT_TRACE_VAL(32, rows);
-  }
-  __syncthreads();
-  ALUT_TRACE(16);
-#endif
   if (L == 64)
     score_row_fixed<TK, 64>(row, ok && tid < rows, qs, cnt, chunk * kSearchChunkK, red_s, red_k);
   else if (L == 128)
@@ -490,7 +488,25 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
     score_row<TK, true>(row, ok && tid < rows, qs, L, cnt, chunk * kSearchChunkK, red_s, red_k);
   __syncthreads();
   ALUT_TRACE(14);
-  fold_slots(cnt, pid, a.idx_offset, a.best, red_s, red_k);
+  if (tid < cnt) {
+    uint64_t b = 0ull;
+#pragma unroll
+    for (int w = 0; w < kSearchThreads / 32; ++w) {
+      const int k = red_k[w][tid];
+      if (k >= 0) {
+        const uint64_t c = pack_cand(red_s[w][tid], a.idx_offset + static_cast<uint32_t>(k));
+        b = c > b ? c : b;
+      }
+    }
+    if (b) {
+      const uint64_t old = atomicMax(reinterpret_cast<unsigned long long*>(a.best + pid[tid]),
+                                     static_cast<unsigned long long>(b));
+      if (d.values && b > old)
+        prefetch_l2_bulk(d.values + static_cast<int64_t>(table >> 1) * d.vs_e + static_cast<int64_t>(table & 1) * d.vs_m +
+                             static_cast<int64_t>(cand_index(b) - a.idx_offset) * d.vs_k,
+                         d.row_bytes);
+    }
+  }
   ALUT_TRACE(15);
 }
 
