@@ -284,6 +284,46 @@ int alut_lookup_combine_noalloc(const alut_tables_t* tables, const alut_batch_t*
                                 uint8_t* out_hit, int64_t* out_idx, int64_t out_stride_hit,
                                 alut_stream_t stream);
 
+/* ---- router prologue (table_moe/ops/qwen_topk_softmax.py:122-153, skip/pruning.py:4-52) ----
+ * Which slots a layer computes; the others are looked up (cached_layers.py:336-337). */
+typedef enum alut_keep_mode {
+  ALUT_KEEP_FIXED = 0,      /* slots [0, keep_k) of every token computed: build_fixed_keep_mask /
+                               build_decode_keep_mask (pruning.py:4-15, :51); keep_k < 0 = all */
+  ALUT_KEEP_IMPORTANCE = 1, /* build_prefill_keep_mask (pruning.py:18-48) */
+} alut_keep_mode_t;
+
+/* Bytes of the workspace of alut_route for num_experts experts (zero-filled once; the
+ * kernels leave it zeroed). 0 for invalid sizes. */
+size_t alut_route_workspace_size(int32_t num_experts);
+
+/* Top-k softmax routing and keep mask of q tokens in one call:
+ *   probabilities = softmax(fp32(logits[t, :num_experts])) (logits f32/bf16/f16, row stride
+ *   logits_stride); weights[t, s], sel[t, s] = the top_k largest in descending order (lower
+ *   expert id first among equal probabilities); with normalize_topk the weights are divided
+ *   by max(their sum, 1e-20) (qwen_topk_softmax.py:150-151);
+ *   compute[t, s] = 1 for computed slots, reuse[t, s] = 1 - compute[t, s] for looked-up ones:
+ *     ALUT_KEEP_FIXED: s < keep_k;
+ *     ALUT_KEEP_IMPORTANCE: expert sel[t, s] is among the first max(1, int(n_active *
+ *       keep_rate)) activated experts ranked by the sum over their slots of
+ *       attn[t] * weights[t, s] (attn != NULL) or weights[t, s] / q (larger sum first, lower
+ *       id on equal sums; sums are accumulated exactly in 2^-40 fixed point, |sum| < 2^23).
+ * Outputs are [q, top_k] with row stride out_stride (elements). top_k <= 64 and
+ * top_k <= num_experts <= 4096. Replaces qwen_topk_softmax followed by _build_compute_mask
+ * (qwen3_vl_moe/cached_layers.py:69-84, :282-286, :336). */
+int alut_route(int32_t q, int32_t num_experts, int32_t top_k, const void* logits, int32_t logits_dtype,
+               int64_t logits_stride, int32_t normalize_topk, int32_t keep_mode, int32_t keep_k,
+               double keep_rate, const float* attn, float* weights, int64_t* sel, uint8_t* compute,
+               uint8_t* reuse, int64_t out_stride, void* workspace, size_t workspace_bytes,
+               alut_stream_t stream);
+
+/* The importance keep mask alone, for routing computed elsewhere (build_prefill_keep_mask,
+ * pruning.py:18-48): sel/weights [q, top_k] (row stride in_stride) in, compute/reuse out
+ * (row stride out_stride), same rule and workspace as alut_route's ALUT_KEEP_IMPORTANCE.
+ * Expert ids outside [0, num_experts) are never kept. */
+int alut_keep_mask(int32_t q, int32_t num_experts, int32_t top_k, const int64_t* sel, const float* weights,
+                   int64_t in_stride, const float* attn, double keep_rate, uint8_t* compute, uint8_t* reuse,
+                   int64_t out_stride, void* workspace, size_t workspace_bytes, alut_stream_t stream);
+
 /* Device-side error bits of a workspace (or, with workspace NULL, of the no-allocation
  * entry point's scratch). Kernels set them and never clear them, so they accumulate over
  * every call that used the workspace until this function clears them (clear != 0). It

@@ -65,3 +65,47 @@ def combined_mismatches(got, ref):
     err = np.abs(got - ref)
     tol = COMBINE_RTOL * np.abs(ref) + COMBINE_RTOL * scale + 1e-12
     return int(np.count_nonzero(err > tol)), float(err.max())
+
+
+ROUTE_W_RTOL = 1e-5
+ROUTE_TIE_RTOL = 1e-6
+ROUTE_SUM_RTOL = 1e-5
+
+
+def route_mismatches(got_w, got_sel, got_keep, ref_w, ref_sel, ref_keep, probs, sums=None, kept=None):
+    """Slots breaking the router rules:
+      * weights within 1e-5 relative (+1e-7) of the reference's;
+      * expert ids equal, except where the two chosen probabilities are within 1e-6
+        relative (the reference's top-k leaves the order of equal values open);
+      * keep mask equal, except on slots whose expert id differs by such a tie, or whose
+        expert's importance sum lies within 1e-5 relative of the sum at the keep boundary
+        (``sums`` per expert and ``kept`` in rank order, importance mode)."""
+    got_w, ref_w = np.asarray(got_w, np.float64), np.asarray(ref_w, np.float64)
+    got_sel, ref_sel = np.asarray(got_sel), np.asarray(ref_sel)
+    bad = []
+    werr = np.abs(got_w - ref_w) > ROUTE_W_RTOL * np.abs(ref_w) + 1e-7
+    for t, s in zip(*np.nonzero(werr)):
+        bad.append(("weight", int(t), int(s), float(got_w[t, s]), float(ref_w[t, s])))
+    tie = np.zeros(got_sel.shape, bool)
+    for t, s in zip(*np.nonzero(got_sel != ref_sel)):
+        pg, pr = float(probs[t, got_sel[t, s]]), float(probs[t, ref_sel[t, s]])
+        if abs(pg - pr) <= ROUTE_TIE_RTOL * max(abs(pr), 1e-30):
+            tie[t, s] = True
+        else:
+            bad.append(("expert", int(t), int(s), int(got_sel[t, s]), int(ref_sel[t, s])))
+    if got_keep is not None:
+        got_keep, ref_keep = np.asarray(got_keep, bool), np.asarray(ref_keep, bool)
+        bounds = []
+        if sums is not None and kept is not None and len(kept):
+            bounds.append(sums[kept[-1]])
+            rest = np.setdiff1d(np.unique(ref_sel), kept)
+            if rest.size:
+                bounds.append(np.max(sums[rest]))
+        for t, s in zip(*np.nonzero(got_keep != ref_keep)):
+            if tie[t, s]:
+                continue
+            e = int(got_sel[t, s])
+            if sums is not None and any(abs(sums[e] - b) <= ROUTE_SUM_RTOL * max(abs(b), 1e-30) for b in bounds):
+                continue
+            bad.append(("keep", int(t), int(s), bool(got_keep[t, s]), bool(ref_keep[t, s])))
+    return bad

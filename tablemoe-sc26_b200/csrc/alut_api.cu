@@ -17,6 +17,7 @@
 #include "alut_project_tc.cuh"
 #include "alut_peer.cuh"
 #include "alut_online.cuh"
+#include "alut_route.cuh"
 
 namespace alut {
 
@@ -776,6 +777,104 @@ int alut_gather_rows_sharded(int32_t n, const uint8_t* hit, const int64_t* idx, 
       shard_stride_m, esz, value_stride_k * esz, static_cast<int>(row_bytes), static_cast<unsigned char*>(out),
       out_stride * esz);
   return check_launch("k_gather_sharded");
+}
+
+size_t alut_route_workspace_size(int32_t num_experts) {
+  if (num_experts <= 0 || num_experts > kRouteMaxExperts) return 0;
+  return align256(sizeof(unsigned long long) * num_experts) + align256(sizeof(int) * num_experts);
+}
+
+int alut_route(int32_t q, int32_t num_experts, int32_t top_k, const void* logits, int32_t logits_dtype,
+               int64_t logits_stride, int32_t normalize_topk, int32_t keep_mode, int32_t keep_k,
+               double keep_rate, const float* attn, float* weights, int64_t* sel, uint8_t* compute,
+               uint8_t* reuse, int64_t out_stride, void* workspace, size_t workspace_bytes,
+               alut_stream_t stream) {
+  if (q < 0 || num_experts <= 0 || top_k <= 0) return fail(ALUT_EINVAL, "route: q=%d experts=%d top_k=%d", q, num_experts, top_k);
+  if (num_experts > kRouteMaxExperts || top_k > kMaxSlots || top_k > num_experts)
+    return fail(ALUT_ERANGE, "route: top_k=%d must be <= min(64, experts) and experts=%d <= %d", top_k, num_experts,
+                kRouteMaxExperts);
+  if (!dtype_ok(logits_dtype)) return fail(ALUT_EDTYPE, "route: logits dtype");
+  if (keep_mode != ALUT_KEEP_FIXED && keep_mode != ALUT_KEEP_IMPORTANCE) return fail(ALUT_EINVAL, "route: keep mode");
+  if (q == 0) return ALUT_OK;
+  if (!logits || !weights || !sel || !compute || !reuse) return fail(ALUT_EINVAL, "route: NULL argument");
+  if (logits_stride < num_experts || out_stride < top_k) return fail(ALUT_ESHAPE, "route: strides");
+  const size_t need = alut_route_workspace_size(num_experts);
+  if (keep_mode == ALUT_KEEP_IMPORTANCE && (!workspace || workspace_bytes < need))
+    return fail(ALUT_EWORKSPACE, "route: workspace has %zu bytes, needs %zu", workspace_bytes, need);
+  if (keep_mode == ALUT_KEEP_IMPORTANCE && !(keep_rate >= 0.0))
+    return fail(ALUT_EINVAL, "route: keep_rate must be >= 0");
+  RouteArgs a{};
+  a.q = q;
+  a.e = num_experts;
+  a.k = top_k;
+  a.logits = logits;
+  a.logits_dtype = logits_dtype;
+  a.logits_stride = logits_stride;
+  a.normalize = normalize_topk;
+  a.mode = keep_mode;
+  a.keep_k = keep_k < 0 ? top_k : std::min(keep_k, top_k);
+  a.keep_rate = keep_rate;
+  a.attn = attn;
+  a.w = weights;
+  a.sel = sel;
+  a.compute = compute;
+  a.reuse = reuse;
+  a.out_stride = out_stride;
+  if (workspace) {
+    a.sums = static_cast<unsigned long long*>(workspace);
+    a.counts = reinterpret_cast<int*>(static_cast<char*>(workspace) + align256(sizeof(unsigned long long) * num_experts));
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t sm = sizeof(float) * kRouteWarps * num_experts;
+  int rc = allow_smem(reinterpret_cast<const void*>(k_route_topk), sm);
+  if (rc) return rc;
+  k_route_topk<<<ceil_div(q, kRouteWarps), kRouteWarps * 32, sm, st>>>(a);
+  rc = check_launch("k_route_topk");
+  if (rc || keep_mode != ALUT_KEEP_IMPORTANCE) return rc;
+  const size_t ks = (sizeof(long long) + sizeof(int) + 1) * static_cast<size_t>(num_experts);
+  rc = allow_smem(reinterpret_cast<const void*>(k_route_keep), ks);
+  if (rc) return rc;
+  k_route_keep<<<1, kRouteKeepThreads, ks, st>>>(a);
+  return check_launch("k_route_keep");
+}
+
+int alut_keep_mask(int32_t q, int32_t num_experts, int32_t top_k, const int64_t* sel, const float* weights,
+                   int64_t in_stride, const float* attn, double keep_rate, uint8_t* compute, uint8_t* reuse,
+                   int64_t out_stride, void* workspace, size_t workspace_bytes, alut_stream_t stream) {
+  if (q < 0 || num_experts <= 0 || top_k <= 0) return fail(ALUT_EINVAL, "keep_mask: sizes");
+  if (num_experts > kRouteMaxExperts) return fail(ALUT_ERANGE, "keep_mask: experts=%d > %d", num_experts, kRouteMaxExperts);
+  if (q == 0) return ALUT_OK;
+  if (!sel || !weights || !compute || !reuse) return fail(ALUT_EINVAL, "keep_mask: NULL argument");
+  if (in_stride < top_k || out_stride < top_k) return fail(ALUT_ESHAPE, "keep_mask: strides");
+  if (!(keep_rate >= 0.0)) return fail(ALUT_EINVAL, "keep_mask: keep_rate must be >= 0");
+  const size_t need = alut_route_workspace_size(num_experts);
+  if (!workspace || workspace_bytes < need)
+    return fail(ALUT_EWORKSPACE, "keep_mask: workspace has %zu bytes, needs %zu", workspace_bytes, need);
+  if (in_stride != out_stride) return fail(ALUT_ESHAPE, "keep_mask: in_stride must equal out_stride");
+  RouteArgs a{};
+  a.q = q;
+  a.e = num_experts;
+  a.k = top_k;
+  a.mode = ALUT_KEEP_IMPORTANCE;
+  a.keep_rate = keep_rate;
+  a.attn = attn;
+  a.w = const_cast<float*>(weights);
+  a.sel = const_cast<int64_t*>(sel);
+  a.compute = compute;
+  a.reuse = reuse;
+  a.out_stride = out_stride;
+  a.sums = static_cast<unsigned long long*>(workspace);
+  a.counts = reinterpret_cast<int*>(static_cast<char*>(workspace) + align256(sizeof(unsigned long long) * num_experts));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t n = static_cast<int64_t>(q) * top_k;
+  k_route_scores<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(a);
+  int rc = check_launch("k_route_scores");
+  if (rc) return rc;
+  const size_t ks = (sizeof(long long) + sizeof(int) + 1) * static_cast<size_t>(num_experts);
+  rc = allow_smem(reinterpret_cast<const void*>(k_route_keep), ks);
+  if (rc) return rc;
+  k_route_keep<<<1, kRouteKeepThreads, ks, st>>>(a);
+  return check_launch("k_route_keep");
 }
 
 int alut_workspace_errors(void* workspace, size_t workspace_bytes, int32_t clear, uint32_t* bits,

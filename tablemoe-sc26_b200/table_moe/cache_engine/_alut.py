@@ -91,6 +91,11 @@ SIGNATURES = {
     "alut_peer_close": (ctypes.c_int, [_P, ctypes.c_uint64]),
     "alut_gather_rows_sharded": (ctypes.c_int, [_I32, _P, _P, _P, _I32, _P, _P, _P, _I64, _I32, _I32, _P, _I64,
                                                 _P]),
+    "alut_route_workspace_size": (_SZ, [_I32]),
+    "alut_route": (ctypes.c_int, [_I32, _I32, _I32, _P, _I32, _I64, _I32, _I32, _I32, ctypes.c_double, _P, _P, _P, _P,
+                                  _P, _I64, _P, _SZ, _P]),
+    "alut_keep_mask": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _I64, _P, ctypes.c_double, _P, _P, _I64, _P, _SZ,
+                                      _P]),
     "alut_workspace_errors": (ctypes.c_int, [_P, _SZ, _I32, ctypes.POINTER(ctypes.c_uint32), _P]),
     "alut_set_profile_events": (ctypes.c_int, [_P, _P]),
     "alut_last_error": (ctypes.c_char_p, []),

@@ -30,7 +30,7 @@ ULP = rules.ULP
 
 def golden_names():
     """Search/combine fixtures (the online-window fixtures are online_*.npz)."""
-    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("online_"))
+    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(("online_", "route_")))
 
 
 def online_names():
@@ -113,3 +113,37 @@ def check_online(got_hit, got_idx, got_slot, ref_hit, ref_idx, ref_slot, scores,
         if got_idx[b] < 0 or ref_idx[b] < 0 or abs(best - chosen) > tol:
             bad.append((b, "idx", int(got_idx[b]), int(ref_idx[b])))
     assert not bad, f"{what}: {bad[:5]}"
+
+
+def route_names():
+    return sorted(p.stem for p in GOLDEN.glob("route_*.npz"))
+
+
+def load_route(name):
+    z = np.load(GOLDEN / f"{name}.npz")
+    meta = json.loads(str(z["meta"]))
+    d = {k: z[k] for k in z.files if k != "meta"}
+    if d["attn"].size == 0:
+        d["attn"] = None
+    return meta, d
+
+
+def route_oracle(meta, d, weights=None, sel=None):
+    """Oracle routing + keep mask of a route fixture (weights/sel: use these instead of the
+    oracle's own top-k, to check a keep mask computed from them)."""
+    import oracle.route as rt
+
+    w, s, p = rt.topk_softmax(d["logits"], meta["k"], meta["normalize"])
+    if weights is not None:
+        w, s = weights, sel
+    sums = kept = None
+    if meta["mode"] == "fixed":
+        keep = rt.fixed_keep_mask(s, meta["keep_k"])
+    else:
+        keep, kept, sums = rt.prefill_keep_mask(s, w, meta["E"], meta["keep_rate"], d["attn"])
+    return w, s, keep, p, sums, kept
+
+
+def check_route(got_w, got_sel, got_keep, ref_w, ref_sel, ref_keep, probs, sums=None, kept=None, what=""):
+    bad = rules.route_mismatches(got_w, got_sel, got_keep, ref_w, ref_sel, ref_keep, probs, sums, kept)
+    assert not bad, f"{what}: {len(bad)} router slots break the rule, first: {bad[:5]}"
