@@ -15,6 +15,12 @@ e2e:   the same through the public LookupStepGraph API with the step's inputs co
        host->device and the outputs device->host inside the graph (pinned buffers).
 --impl reference: the CPU oracle (a restatement of the reference's torch path) on the
        host cores, over a bounded sample of the same workload.
+workloads: the other BASELINE configs, each timed with L2 flushed between steps and each
+       with a roofline: config 1 (single table), config 3 (prefill layer), config 4
+       (DeepSeek-VL2 prefill + decode) and config 5 (the sharded large table, at every N).
+parity: before the JSON line is printed, the checker leg compares a sample of what was
+       timed (layers of the replayed decode graph, tokens of each workload) with the CPU
+       oracle (test infrastructure) and reports the mismatches.
 
 N>1: one process per GPU, each a replica with its own tables and token batch (the decode
 lookup does not shard: "replicas only"); value is the sum over ranks of lookups divided
@@ -45,10 +51,34 @@ METRIC = "ALUT lookups/s (token-expert pairs)"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 KERNELS_PER_LAYER = 3  # project+plan, centroid scan, gather/combine
 CPU_LAYERS = 4
-PROFILE_STEPS = 20  # replays of the event-instrumented step graph for the scan-kernel timing
-# DRAM bytes (read + write) per layer of k_project_mma + k_search_decode, from one ncu
-# capture of this workload's layer shape (profiles/decode_kernels_full_qwen3vl_c2.md).
-NCU_TRAFFIC_PER_LAYER = 1_698_048 + 12_360_448
+CSRC = ROOT / "tablemoe-sc26_b200" / "csrc"
+TRAFFIC_FILE = ROOT / "profiles" / "decode_layer_dram_traffic_qwen3vl_c2.txt"
+
+
+def source_digest():
+    """sha256 over the kernel sources and the header: names the build a capture was made of."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for f in sorted(CSRC.glob("*.cu*")) + [ROOT / "include" / "alut.h"]:
+        h.update(f.name.encode())
+        h.update(f.read_bytes())
+    return h.hexdigest()
+
+
+def ncu_traffic():
+    """DRAM bytes (read + write) of one decode layer's three kernels from the committed ncu
+    summary, when it was captured from these exact sources; else None."""
+    if not TRAFFIC_FILE.exists():
+        return None, "no capture committed"
+    kv = {}
+    for line in TRAFFIC_FILE.read_text().splitlines():
+        if ":" in line:
+            k, v = line.split(":", 1)
+            kv[k.strip()] = v.strip()
+    if kv.get("source_sha256") != source_digest():
+        return None, "committed capture is of other kernel sources"
+    return int(kv["dram_bytes_per_layer"]), "ncu capture of this build (" + TRAFFIC_FILE.name + ")"
 
 
 def dist_env():
@@ -186,12 +216,16 @@ def max_over_ranks(v, world, device):
     return float(t.item())
 
 
-# ---- secondary workloads: prefill layer (config 3) and the sharded large table (config 5) ----
+# ---- secondary workloads: the other BASELINE configs --------------------------------------
 # Reported under "workloads" in the same JSON line; the headline value stays the decode step.
 
+C1 = dict(tokens=256, k=256, l=64, h=2048)
 C3 = dict(tokens=4096, vision_tokens=1024, experts=128, k=1024, l=64, h=2048, top_k=8, lookup_frac=0.4, zipf=1.1)
+C4 = dict(layers=30, experts=72, top_k=6, k=2048, l=96, h=2560, prefill_tokens=2048, decode_steps=64,
+          decode_batch=8, lookup_frac=0.4)
 C5 = dict(tokens=32768, k=65536, l=128, h=4096)
 L2_FLUSH_BYTES = 256 << 20  # written between timed steps (L2 is 126 MB)
+SAMPLE_TOKENS = 512         # tokens of a large batch the checker leg compares with the oracle
 
 
 def orthonormal_basis(h, l, g, device):
@@ -221,23 +255,155 @@ def timed_steps(fn, steps, warmup, device, flush, events=None):
     return total, (sum(scan) / len(scan) if scan else None)
 
 
-def with_scan_events(lib):
-    """CUDA events registered as the library's profile events (they bracket the scan)."""
-    import ctypes
+def hbm_roofline(kernel, nbytes, seconds, peaks, **extra):
+    gbs = nbytes / seconds / 1e9
+    return {"kernel": kernel, "bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(gbs / peaks["hbm_gbs"], 4), "bytes_per_launch": int(nbytes),
+            "launch_us": round(seconds * 1e6, 3), **extra}
 
-    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-    ev[0].record()
-    ev[1].record()
+
+def tensor_roofline(kernel, flops, seconds, peaks, **extra):
+    tf = flops / seconds / 1e12
+    return {"kernel": kernel, "bound": "tensor", "achieved": round(tf, 2), "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_tflops"], 4), "flops_per_launch": int(flops),
+            "launch_us": round(seconds * 1e6, 3), **extra}
+
+
+# ---- checker leg (test infrastructure: the CPU oracle checks a sample of what was timed) ----
+
+class Checker:
+    """Counts slots and elements of the timed outputs that break the parity rules of
+    oracle/parity_rules.py (indices exact except near ties, rows exact, combine within 1e-2)."""
+
+    def __init__(self):
+        self.results = {}
+
+    def _add(self, name, checked, bad, exempt=0):
+        r = self.results.setdefault(name, {"checked": 0, "mismatches": 0, "exempt": 0})
+        r["checked"] += int(checked)
+        r["mismatches"] += int(bad)
+        r["exempt"] += int(exempt)
+
+    def lookup(self, name, *, x, vis, proj, bias, keys, sel, reuse, weights, compute, values_bits, hit, idx, out,
+               renorm, cmp_ge, thr, normalize=False, accumulate_base=None):
+        """Oracle project + search + combine of one batch (numpy inputs) against the GPU's
+        hit / idx / out for the same batch."""
+        import oracle.oracle as orc
+        import oracle.parity_rules as rules
+
+        q = orc.project(x, vis, proj, bias, normalize=normalize)
+        rh, ri, _, _ = orc.search(q, keys, sel, vis, reuse, thr, thr, cmp_ge=cmp_ge, with_gap=False)
+        bad, exempt = rules.search_mismatches(hit, idx, rh, ri, q, keys, sel, vis, (thr, thr), "float32")
+        self._add(name, sel.size, len(bad), exempt)
+        ref = orc.combine(values_bits, sel, vis, hit, idx, weights, compute=compute, renorm=renorm,
+                          out=accumulate_base)
+        n, _ = rules.combined_mismatches(out, ref)
+        self._add(name, 0, n)
+
+    def rows(self, name, got, ref):
+        """got / ref: bit patterns of the rows (uint16)."""
+        bad = int(np.count_nonzero(np.any(got != ref, axis=1)))
+        self._add(name, got.shape[0], bad)
+
+    def search_only(self, name, *, q, keys, sel, vis, hit, idx, thr, cmp_ge):
+        import oracle.oracle as orc
+        import oracle.parity_rules as rules
+
+        rh, ri, _, _ = orc.search(q, keys, sel, vis, None, thr, thr, cmp_ge=cmp_ge, with_gap=False)
+        bad, exempt = rules.search_mismatches(hit, idx, rh, ri, q, keys, sel, vis, (thr, thr), "float32")
+        self._add(name, sel.size, len(bad), exempt)
+
+    def summary(self):
+        tot = {"checked": 0, "mismatches": 0, "exempt": 0}
+        for r in self.results.values():
+            for k in tot:
+                tot[k] += r[k]
+        return {**tot, "per_workload": self.results,
+                "rule": "indices exact except near ties (1e-5 rel), rows bit-exact, combine within 1e-2 rel"}
+
+
+def bits16(t):
+    return t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def basis_np(mgr):
+    proj = np.stack([mgr.pca["vision"]["proj"].cpu().numpy(), mgr.pca["text"]["proj"].cpu().numpy()])
+    bias = np.stack([mgr.pca["vision"]["bias"].cpu().numpy(), mgr.pca["text"]["bias"].cpu().numpy()])
+    return proj, bias
+
+
+def check_engine_lookup(checker, name, mgr, x, sel, vis, reuse, w, comp, hit, idx, out, *, variant, renorm,
+                        rows=None, keys=None):
+    """Checker of one lookup_combine batch (device tensors), optionally on a row subset."""
+    rows = slice(None) if rows is None else rows
+    cmp_ge, thr, keyset = {"decode": (True, 0.0, "norm"), "prefill_dot": (False, 0.0, "raw"),
+                           "decode_dot": (False, 0.0, "raw")}[variant]
+    if keys is None:
+        keys = (mgr.keys_buffer if keyset == "norm" else mgr.raw_keys_buffer).float().cpu().numpy()
+    proj, bias = basis_np(mgr)
+    rn = {"none": 0, "to_one": 1, "to_rowsum": 2}[renorm]
+    checker.lookup(name, x=x[rows].float().cpu().numpy(), vis=vis[rows].cpu().numpy(), proj=proj, bias=bias,
+                   keys=keys, sel=sel[rows].cpu().numpy(), reuse=reuse[rows].cpu().numpy(),
+                   weights=w[rows].float().cpu().numpy(), compute=None if comp is None else comp[rows].cpu().numpy(),
+                   values_bits=bits16(mgr.values_buffer), hit=hit[rows].cpu().numpy(), idx=idx[rows].cpu().numpy(),
+                   out=out[rows].float().cpu().numpy(), renorm=rn, cmp_ge=cmp_ge, thr=thr)
+    return keys
+
+
+def c1_workload(args, device, flush, peaks, checker):
+    """One table (K=256, L=64 fp32, 256 x 2048 bf16 rows), 256 tokens of hidden 2048, every
+    token looked up (dot rule), rows scaled by U(0,1) weights and accumulated into the
+    output (no renormalisation). The call is replayed as a one-layer CUDA graph."""
+    from table_moe.cache_engine import HybridStorageManager, VectorSearchEngine
+    from table_moe.cache_engine.step_graph import LookupStepGraph
+
+    c = C1
+    g = torch.Generator(device=device).manual_seed(1001)
+    x = torch.randn(c["tokens"], c["h"], generator=g, device=device).to(torch.bfloat16)
+    proj = orthonormal_basis(c["h"], c["l"], g, device)
+    keys = torch.randn(1, 2, c["k"], c["l"], generator=g, device=device)
+    values = torch.randn(1, 2, c["k"], c["h"], generator=g, device=device, dtype=torch.bfloat16).mul_(0.05)
+    w = torch.rand(c["tokens"], 1, generator=g, device=device)
+    pca = {m: {"proj": proj, "bias": torch.zeros(c["l"], device=device)} for m in ("vision", "text")}
+    mgr = HybridStorageManager.from_tables(0, keys, values, pca, keys=keys)
+    gr = LookupStepGraph([VectorSearchEngine(mgr)], c["tokens"], 1, variant="prefill_dot", renorm="none",
+                         keep_hits=True)
+    b = gr.layers[0]
+    b.x.copy_(x)
+    b.sel.zero_()
+    b.is_vision.zero_()
+    b.reuse.fill_(True)
+    b.weights.copy_(w)
+    b.compute.zero_()
+    gr.capture()
+    total_ms, _ = timed_steps(gr.replay, args.wl_steps, args.warmup, device, flush)
+    b.out.zero_()
+    gr.replay()
     torch.cuda.synchronize()
-    lib.alut_set_profile_events(ctypes.c_void_p(ev[0].cuda_event), ctypes.c_void_p(ev[1].cuda_event))
-    return ev
+    hit, idx, out = gr.hits[0], gr.idx[0], b.out
+    check_engine_lookup(checker, "c1", mgr, b.x, b.sel, b.is_vision, b.reuse, b.weights, None, hit, idx, out,
+                        variant="prefill_dot", renorm="none")
+    hits = int(hit.sum())
+    nbytes = x.numel() * 2 + c["h"] * c["l"] * 4 + c["k"] * c["l"] * 4 + hits * c["h"] * 2 + 2 * out.numel() * 2
+    t = total_ms / args.wl_steps / 1e3
+    return {
+        "config": "BASELINE config 1: one table K=256, L=64 fp32, 256x2048 bf16 rows, 256 tokens (hidden 2048), "
+                  "dot rule, U(0,1) weights, rows accumulated into the output",
+        "value": round(c["tokens"] / t, 1), "unit": "lookups/s", "ms_per_step": round(t * 1e3, 4),
+        "steps": args.wl_steps, "l2": "flushed between steps (256 MB write outside the timed span)",
+        "roofline": hbm_roofline("one alut_lookup_combine call (plan, projection, scan, combine; graph replay)",
+                                 nbytes, t, peaks,
+                                 bytes_note="x + text basis + table keys + hit rows + output read/write"),
+    }
 
 
-def c3_workload(args, device, flush, peaks):
+def c3_workload(args, device, flush, peaks, checker):
     """One Qwen3-VL prefill layer: 4096 tokens (first 1024 image tokens ~ N(0.5, 1)), Zipf(1.1)
     top-8 routing over 128 experts, 40% of the routed slots looked up; search (raw keys,
-    dot, the reference's default prefill strategy) + weighted combine of the hits."""
-    from table_moe.cache_engine import HybridStorageManager, VectorSearchEngine, _alut
+    dot, the reference's default prefill strategy) + weighted combine of the hits, replayed
+    as a one-layer CUDA graph."""
+    from table_moe.cache_engine import HybridStorageManager, VectorSearchEngine
+    from table_moe.cache_engine.step_graph import LookupStepGraph
 
     c = C3
     g = torch.Generator(device=device).manual_seed(3003)
@@ -245,7 +411,7 @@ def c3_workload(args, device, flush, peaks):
     values = torch.randn(c["experts"], 2, c["k"], c["h"], generator=g, device=device, dtype=torch.bfloat16).mul_(0.05)
     pca = {m: {"proj": orthonormal_basis(c["h"], c["l"], g, device), "bias": torch.zeros(c["l"], device=device)}
            for m in ("vision", "text")}
-    mgr = HybridStorageManager.from_tables(0, raw, values, pca)
+    mgr = HybridStorageManager.from_tables(0, raw, values, pca, keys=raw)
     q = c["tokens"]
     x = torch.randn(q, c["h"], generator=g, device=device)
     x[:c["vision_tokens"]] += 0.5
@@ -257,50 +423,177 @@ def c3_workload(args, device, flush, peaks):
     reuse = torch.rand(q, c["top_k"], generator=g, device=device) < c["lookup_frac"]
     comp = ~reuse
     eng = VectorSearchEngine(mgr)
-    out = torch.empty(q, c["h"], dtype=torch.bfloat16, device=device)
-
-    def step():
-        out.zero_()
-        eng.lookup_combine(x, sel, vis, reuse, w, compute_mask=comp, out=out, variant="prefill_dot")
-
-    lib = _alut.load()
-    total_ms, _ = timed_steps(step, args.wl_steps, args.warmup, device, flush)
-    ev = with_scan_events(lib)
-    _, scan_ms = timed_steps(step, 10, 1, device, flush, events=ev)
-    lib.alut_set_profile_events(None, None)
+    graphs = []
+    for prof in (False, True):  # the timed graph, and a twin whose scan is bracketed by events
+        gr = LookupStepGraph([eng], q, c["top_k"], variant="prefill_dot", renorm="to_one", keep_hits=True)
+        b = gr.layers[0]
+        for name, t in (("x", x), ("sel", sel), ("is_vision", vis), ("reuse", reuse), ("weights", w),
+                        ("compute", comp)):
+            getattr(b, name).copy_(t)
+        ev = None
+        if prof:
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))]
+            for e in ev[0]:
+                e.record()
+            torch.cuda.synchronize()
+        gr.capture(profile_events=ev)
+        graphs.append(gr)
+    total_ms, _ = timed_steps(graphs[0].replay, args.wl_steps, args.warmup, device, flush)
+    scan = []
+    for _ in range(10):
+        flush.fill_(1)
+        graphs[1].replay()
+        torch.cuda.synchronize()
+        scan += graphs[1].scan_times_ms()
+    scan_ms = sum(scan) / len(scan)
+    gr = graphs[0]
+    b = gr.layers[0]
+    b.out.zero_()
+    gr.replay()
+    torch.cuda.synchronize()
+    rows = torch.randperm(q, generator=torch.Generator().manual_seed(3))[:SAMPLE_TOKENS].sort().values
+    check_engine_lookup(checker, "c3", mgr, b.x, b.sel, b.is_vision, b.reuse, b.weights, b.compute, gr.hits[0],
+                        gr.idx[0], b.out, variant="prefill_dot", renorm="to_one", rows=rows.to(device))
     pairs = int(reuse.sum())
     tables = len(set((sel[reuse] * 2 + (~vis).long()[:, None].expand_as(sel)[reuse]).tolist()))
     flops = pairs * c["k"] * c["l"] * 2
     key_bytes = tables * c["k"] * c["l"] * 2  # bf16 operand form of every routed table, once
-    achieved = flops / (scan_ms / 1e3) / 1e12
     return {
         "config": "BASELINE config 3: qwen3-vl prefill layer, 4096 tokens, 128 experts, Zipf(1.1) top-8, "
                   "K=1024, L=64, 40% looked up (prefill_dot)",
         "value": round(pairs * args.wl_steps / (total_ms / 1e3), 1), "unit": "lookups/s",
         "ms_per_step": round(total_ms / args.wl_steps, 4), "lookups_per_step": pairs, "steps": args.wl_steps,
         "l2": "flushed between steps (256 MB write outside the timed span)",
-        "roofline": {"kernel": "k_search_tc (tcgen05 centroid scan)", "bound": "tensor",
-                     "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": round(achieved / peaks["bf16_tflops"], 4), "flops_per_launch": flops,
-                     "launch_us": round(scan_ms * 1e3, 2),
-                     "key_bytes_per_launch": key_bytes,
-                     "hbm_frac": round(key_bytes / (scan_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)},
+        "roofline": tensor_roofline("k_search_tc (tcgen05 centroid scan; event nodes around it in a twin graph)",
+                                    flops, scan_ms / 1e3, peaks,
+                                    key_bytes_per_launch=key_bytes,
+                                    hbm_frac=round(key_bytes / (scan_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)),
     }
 
 
-def c5_workload(args, rank, world, device, flush, peaks):
+def c4_build(device):
+    """30 DeepSeek-VL2-shaped layers (72 routed experts, K=2048, L=96 fp32 keys, 2560-wide
+    bf16 rows) and the routing of a 2048-token prefill and of a batch of 8 decode tokens."""
+    from table_moe.cache_engine import HybridStorageManager
+
+    c = C4
+    mgrs, pre, dec = [], [], []
+    for li in range(c["layers"]):
+        g = torch.Generator(device=device).manual_seed(40000 + li)
+        raw = torch.randn(c["experts"], 2, c["k"], c["l"], generator=g, device=device)
+        values = torch.randn(c["experts"], 2, c["k"], c["h"], generator=g, device=device,
+                             dtype=torch.bfloat16).mul_(0.05)
+        pca = {m: {"proj": orthonormal_basis(c["h"], c["l"], g, device), "bias": torch.zeros(c["l"], device=device)}
+               for m in ("vision", "text")}
+        mgrs.append(HybridStorageManager.from_tables(li, raw, values, pca, keys=raw, enable_online=False))
+        for n, dst in ((c["prefill_tokens"], pre), (c["decode_batch"], dec)):
+            x = torch.randn(n, c["h"], generator=g, device=device).to(torch.bfloat16)
+            w, sel = torch.topk(torch.softmax(torch.randn(n, c["experts"], generator=g, device=device), -1),
+                                c["top_k"], dim=-1)
+            reuse = torch.rand(n, c["top_k"], generator=g, device=device) < c["lookup_frac"]
+            dst.append(dict(x=x, sel=sel, is_vision=torch.zeros(n, dtype=torch.bool, device=device), reuse=reuse,
+                            weights=w.float(), compute=~reuse))
+    return mgrs, pre, dec
+
+
+def layer_bytes(inp, k, l, h, with_out=True):
+    """Algorithmic bytes of one lookup batch: distinct routed tables' keys, the basis of the
+    modalities present, x, the looked-up rows and the output read + write."""
+    r = inp["reuse"]
+    m = (~inp["is_vision"]).long()[:, None].expand_as(inp["sel"])
+    tables = int(torch.unique((inp["sel"] * 2 + m)[r]).numel())
+    mods = int(inp["is_vision"].any()) + int((~inp["is_vision"]).any())
+    n = int(r.sum())
+    return tables * k * l * 4 + mods * h * l * 4 + inp["x"].numel() * 2 + n * h * 2 + \
+        (2 * inp["x"].numel() * 2 if with_out else 0), n
+
+
+def c4_workload(args, device, flush, peaks, checker):
+    """DeepSeek-VL2: a 2048-token prefill through 30 layers, then 64 decode steps of batch 8
+    through the same 30 layers (dot rule, renormalised to the row sum of the routing
+    weights, deepseek_layers.py:707-729). One step = the prefill + the 64 decode steps."""
+    from table_moe.cache_engine import VectorSearchEngine
+    from table_moe.cache_engine.step_graph import LookupStepGraph
+
+    c = C4
+    mgrs, pre, dec = c4_build(device)
+    engines = [VectorSearchEngine(m) for m in mgrs]
+    graphs = {}
+    for name, q, inputs, variant in (("prefill", c["prefill_tokens"], pre, "prefill_dot"),
+                                     ("decode", c["decode_batch"], dec, "decode_dot")):
+        gr = LookupStepGraph(engines, q, c["top_k"], variant=variant, renorm="to_rowsum", keep_hits=True)
+        for b, inp in zip(gr.layers, inputs):
+            for k2, t in inp.items():
+                getattr(b, k2).copy_(t)
+        gr.capture()
+        graphs[name] = gr
+
+    def prefill():
+        graphs["prefill"].replay()
+
+    def decode():
+        for _ in range(c["decode_steps"]):
+            graphs["decode"].replay()
+
+    def step():
+        prefill()
+        decode()
+
+    total_ms, _ = timed_steps(step, args.wl_steps, args.warmup, device, flush)
+    pre_ms, _ = timed_steps(prefill, args.wl_steps, 2, device, flush)
+    dec_ms, _ = timed_steps(decode, args.wl_steps, 2, device, flush)
+    # Checker: one fresh replay of each graph, layers 0 and 29 (prefill on a token sample).
+    for gr in graphs.values():
+        for b in gr.layers:
+            b.out.zero_()
+        gr.replay()
+    torch.cuda.synchronize()
+    rows = torch.randperm(c["prefill_tokens"], generator=torch.Generator().manual_seed(4))[:SAMPLE_TOKENS]
+    rows = rows.sort().values.to(device)
+    for li in (0, c["layers"] - 1):
+        for name, inputs, rr in (("prefill", pre, rows), ("decode", dec, None)):
+            gr, inp = graphs[name], inputs[li]
+            check_engine_lookup(checker, f"c4_{name}", mgrs[li], inp["x"], inp["sel"], inp["is_vision"],
+                                inp["reuse"], inp["weights"], inp["compute"], gr.hits[li], gr.idx[li],
+                                gr.layers[li].out, variant="prefill_dot" if name == "prefill" else "decode_dot",
+                                renorm="to_rowsum", rows=rr)
+    pre_lookups = sum(int(i["reuse"].sum()) for i in pre)
+    dec_lookups = sum(int(i["reuse"].sum()) for i in dec) * c["decode_steps"]
+    dec_bytes = sum(layer_bytes(i, c["k"], c["l"], c["h"])[0] for i in dec) * c["decode_steps"]
+    pre_flops = pre_lookups * c["k"] * c["l"] * 2
+    t_step, t_pre, t_dec = (v / args.wl_steps / 1e3 for v in (total_ms, pre_ms, dec_ms))
+    return {
+        "config": "BASELINE config 4: deepseek-vl2, 30 layers x 72 routed experts top-6, K=2048, L=96 fp32, "
+                  "2560-wide bf16 rows; 2048-token prefill then 64 decode steps at batch 8; 40% looked up; "
+                  "dot rule, renormalised to the routing row sum",
+        "value": round((pre_lookups + dec_lookups) / t_step, 1), "unit": "lookups/s",
+        "ms_per_step": round(t_step * 1e3, 4), "lookups_per_step": pre_lookups + dec_lookups,
+        "steps": args.wl_steps, "l2": "flushed between steps (256 MB write outside the timed span); a decode "
+        "step touches about 0.4 GB of tables",
+        "prefill": {"ms": round(t_pre * 1e3, 4), "lookups": pre_lookups, "value": round(pre_lookups / t_pre, 1),
+                    "whole_prefill_tensor": tensor_roofline("30-layer prefill (projection, plan, tcgen05 scan, "
+                                                            "combine) over its whole time", pre_flops, t_pre, peaks)},
+        "decode": {"ms_per_decode_step": round(t_dec * 1e3 / c["decode_steps"], 4), "lookups": dec_lookups,
+                   "value": round(dec_lookups / t_dec, 1),
+                   "roofline": hbm_roofline("30-layer decode step (project -> scan -> combine per layer, PDL)",
+                                            dec_bytes / c["decode_steps"], t_dec / c["decode_steps"], peaks)},
+    }
+
+
+def c5_workload(args, rank, world, device, flush, peaks, checker):
     """The large single table (K=65536, L=128 fp32 keys, 65536 x 4096 bf16 rows) sharded by
     centroid range over the ranks; 32768 tokens (hidden 4096, bf16) looked up per step:
-    local tensor-core scan, NCCL all-gather of packed candidates, merge, owner gather and
-    reduce-scatter of the rows. Strong scaling: the same tokens and table at every N."""
+    local tensor-core scan, NCCL all-gather of packed candidates, merge, owner gather.
+    Strong scaling: the same tokens and table at every N."""
     from table_moe.cache_engine.sharded import ShardedCentroidTable, shard_range
 
     c = C5
     k0, k1 = shard_range(c["k"], world, rank)
     g = torch.Generator(device=device).manual_seed(5005)  # identical on every rank
-    keys = torch.randn(1, 2, c["k"], c["l"], generator=g, device=device)[:, :, k0:k1].contiguous()
-    pca = {m: {"proj": orthonormal_basis(c["h"], c["l"], g, device), "bias": torch.zeros(c["l"], device=device)}
-           for m in ("vision", "text")}
+    keys_full = torch.randn(1, 2, c["k"], c["l"], generator=g, device=device)
+    keys = keys_full[:, :, k0:k1].contiguous()
+    proj = [orthonormal_basis(c["h"], c["l"], g, device) for _ in range(2)]
+    pca = {m: {"proj": proj[i], "bias": torch.zeros(c["l"], device=device)} for i, m in enumerate(("vision", "text"))}
     x = torch.randn(c["tokens"], c["h"], generator=g, device=device).to(torch.bfloat16)
     vis = torch.zeros(c["tokens"], dtype=torch.bool, device=device)
     gv = torch.Generator(device=device).manual_seed(6006 + rank)
@@ -313,17 +606,48 @@ def c5_workload(args, rank, world, device, flush, peaks):
     barrier(world)
     total_ms, _ = timed_steps(step, args.wl_steps, args.warmup, device, flush)
     total_ms = max_over_ranks(total_ms, world, device)
+    # Checker: the winners of a token sample against the oracle over the full table, and the
+    # rows of this rank's sampled tokens against the owning shard's (regenerated) values.
+    hit, idx, rows = table.lookup(x, vis)
+    torch.cuda.synchronize()
+    n = c["tokens"] // world
+    lo = rank * n
+    sample = torch.randperm(c["tokens"], generator=torch.Generator().manual_seed(5))[:256].sort().values
+    if rank == 0:
+        import oracle.oracle as orc
+
+        xs = x[sample].float().cpu().numpy()
+        pr = np.stack([p.cpu().numpy() for p in proj])
+        q = orc.project(xs, np.zeros(len(sample), bool), pr, np.zeros((2, c["l"]), np.float32))
+        checker.search_only("c5", q=q, keys=keys_full.cpu().numpy(), sel=np.zeros((len(sample), 1), np.int64),
+                            vis=np.zeros(len(sample), bool), hit=hit[sample].cpu().numpy()[:, None],
+                            idx=idx[sample].cpu().numpy()[:, None], thr=0.0, cmp_ge=False)
+    mine = sample[(sample >= lo) & (sample < lo + n)]
+    ref = torch.zeros(len(mine), c["h"], dtype=torch.bfloat16, device=device)
+    gi = idx[mine.to(device)]
+    for r in range(world):
+        r0, r1 = shard_range(c["k"], world, r)
+        own = hit[mine.to(device)] & (gi >= r0) & (gi < r1)
+        if own.any():
+            gr = torch.Generator(device=device).manual_seed(6006 + r)
+            vr = values if r == rank else torch.randn(1, 2, r1 - r0, c["h"], generator=gr, device=device,
+                                                      dtype=torch.bfloat16).mul_(0.05)
+            ref[own] = vr[0, 1, gi[own] - r0]
+            del vr
+    checker.rows("c5", bits16(rows[(mine - lo).to(device)]), bits16(ref))
+    table.close()
     flops = c["tokens"] * c["k"] * c["l"] * 2
-    achieved = flops / (total_ms / args.wl_steps / 1e3) / 1e12
+    t = total_ms / args.wl_steps / 1e3
+    achieved = flops / t / 1e12
     return {
         "config": "BASELINE config 5: one table K=65536, L=128 fp32, 65536x4096 bf16 rows, 32768 tokens "
                   "(hidden 4096), centroid-range shards over the ranks",
-        "value": round(c["tokens"] * args.wl_steps / (total_ms / 1e3), 1), "unit": "lookups/s",
-        "ms_per_step": round(total_ms / args.wl_steps, 4), "steps": args.wl_steps, "scaling": "strong",
+        "value": round(c["tokens"] / t, 1), "unit": "lookups/s",
+        "ms_per_step": round(t * 1e3, 4), "steps": args.wl_steps, "scaling": "strong",
         "shards": world, "l2": "flushed between steps (256 MB write outside the timed span)",
         "whole_step_tensor": {"achieved": round(achieved, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                              "frac": round(achieved / peaks["bf16_tflops"], 4),
-                              "flops": "tokens x K x L x 2 (scan only) over the whole step time"},
+                              "frac_per_gpu": round(achieved / world / peaks["bf16_tflops"], 4),
+                              "flops": "tokens x K x L x 2 (scan only) over the whole step time, all GPUs"},
     }
 
 
@@ -336,9 +660,8 @@ def cpu_sample(managers, inputs):
     sample = []
     for m, inp in zip(managers, inputs):
         keys = m.keys_buffer.float().cpu().numpy()
-        vals = m.values_buffer.cpu().view(torch.int16).numpy().view(np.uint16)
-        proj = np.stack([m.pca["vision"]["proj"].cpu().numpy(), m.pca["text"]["proj"].cpu().numpy()])
-        bias = np.stack([m.pca["vision"]["bias"].cpu().numpy(), m.pca["text"]["bias"].cpu().numpy()])
+        vals = bits16(m.values_buffer)
+        proj, bias = basis_np(m)
         d = {k: v.numpy() for k, v in inp.items() if k != "x"}
         d["x"] = inp["x"].float().numpy()
         sample.append((keys, vals, proj, bias, d))
@@ -411,9 +734,9 @@ def main():
     ap.add_argument("--impl", choices=["alut", "reference"], default="alut")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--wl-steps", type=int, default=20, help="timed steps of each secondary workload")
-    ap.add_argument("--no-workloads", action="store_true", help="skip the config 3 / config 5 measurements")
-    ap.add_argument("--only", choices=["c3", "c5"], default=None,
+    ap.add_argument("--wl-steps", type=int, default=10, help="timed steps of each secondary workload")
+    ap.add_argument("--no-workloads", action="store_true", help="skip the config 1/3/4/5 measurements")
+    ap.add_argument("--only", choices=["c1", "c3", "c4", "c5"], default=None,
                     help="run only that secondary workload and print its JSON (profiling captures)")
     ap.add_argument("--layers", type=int, default=CFG["layers"],
                     help="fewer layers for profiling captures only (the benchmark is 48)")
@@ -434,10 +757,12 @@ def main():
         elif args.only:
             peaks, _ = measured_peaks()
             flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
-            res = (c3_workload(args, device, flush, peaks) if args.only == "c3"
-                   else c5_workload(args, rank, world, device, flush, peaks))
+            checker = Checker()
+            fn = {"c1": c1_workload, "c3": c3_workload, "c4": c4_workload}.get(args.only)
+            res = fn(args, device, flush, peaks, checker) if fn else \
+                c5_workload(args, rank, world, device, flush, peaks, checker)
             if rank == 0:
-                print(json.dumps({"workload": args.only, **res}), flush=True)
+                print(json.dumps({"workload": args.only, **res, "parity": checker.summary()}), flush=True)
         else:
             run_alut(args, rank, world, local, device)
     finally:
@@ -448,34 +773,28 @@ def main():
 
 
 def run_alut(args, rank, world, local, device):
+    import gc
+
     from table_moe.cache_engine import VectorSearchEngine
     from table_moe.cache_engine.step_graph import LookupStepGraph
 
+    checker = Checker()
     managers = [build_layer(li, device, rank) for li in range(CFG["layers"])]
     engines = [VectorSearchEngine(m) for m in managers]
     inputs = [layer_inputs(li, rank) for li in range(CFG["layers"])]
     torch.cuda.synchronize()
     per_layer = [algorithmic_bytes(inp) for inp in inputs]
-    scan_bytes = [p[0] for p in per_layer]
     path_bytes = sum(p[1] for p in per_layer)
     lookups_per_step = sum(p[2] for p in per_layer)
 
-    # Device-resident step (timed), and a twin graph whose scan launches are bracketed by
-    # event nodes (replayed after the timed region to time the scan kernels; event nodes
-    # break the programmatic overlap between kernels, so they stay out of the timed graph).
-    step = LookupStepGraph(engines, CFG["tokens"], CFG["top_k"], variant="decode", renorm="to_one")
-    prof = LookupStepGraph(engines, CFG["tokens"], CFG["top_k"], variant="decode", renorm="to_one")
-    for g in (step, prof):
-        for b, inp in zip(g.layers, inputs):
-            for name, t in inp.items():
-                getattr(b, name).copy_(t)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in engines]
-    for a, b in ev:  # the CUDA events must exist before capture
-        a.record()
-        b.record()
+    # Device-resident step: the 48 per-layer lookups captured as one CUDA graph (hits and
+    # indices are kept in device buffers for the checker: 16 x 8 entries per layer).
+    step = LookupStepGraph(engines, CFG["tokens"], CFG["top_k"], variant="decode", renorm="to_one", keep_hits=True)
+    for b, inp in zip(step.layers, inputs):
+        for name, t in inp.items():
+            getattr(b, name).copy_(t)
     torch.cuda.synchronize()
     step.capture()
-    prof.capture(profile_events=ev)
     for _ in range(args.warmup):
         step.replay()
     torch.cuda.synchronize()
@@ -493,11 +812,6 @@ def run_alut(args, rank, world, local, device):
     ms_per_step = dev_ms / args.steps
     total_lookups = sum_over_ranks(lookups_per_step, world, device) * args.steps
     value = total_lookups / (dev_ms / 1e3)
-    scan_ms = []
-    for _ in range(PROFILE_STEPS):
-        prof.replay()
-        torch.cuda.synchronize()
-        scan_ms += prof.scan_times_ms()
 
     # End to end through the public API: H2D inputs + lookups + D2H outputs per step.
     e2e = LookupStepGraph(engines, CFG["tokens"], CFG["top_k"], variant="decode", renorm="to_one")
@@ -516,20 +830,32 @@ def run_alut(args, rank, world, local, device):
     t2.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(s2.elapsed_time(t2), world, device)
+    e2e_io = (e2e.h2d_bytes, e2e.d2h_bytes)
+
+    # Checker leg: one fresh replay of the timed graph, three layers against the oracle.
+    for b in step.layers:
+        b.out.zero_()
+    step.replay()
+    torch.cuda.synchronize()
+    for li in (0, CFG["layers"] // 2, CFG["layers"] - 1):
+        if li >= CFG["layers"]:
+            continue
+        inp = {k: v.to(device) for k, v in inputs[li].items()}
+        check_engine_lookup(checker, "c2", managers[li], inp["x"], inp["sel"], inp["is_vision"], inp["reuse"],
+                            inp["weights"], inp["compute"], step.hits[li], step.idx[li], step.layers[li].out,
+                            variant="decode", renorm="to_one")
 
     peaks, peak_src = measured_peaks()
-    roofline = None
-    if scan_ms:
-        avg_ms = sum(scan_ms) / len(scan_ms)
-        bpl = sum(scan_bytes) / len(scan_bytes)
-        achieved = bpl / (avg_ms / 1e3) / 1e9
-        roofline = {"kernel": "k_project + k_search_decode (projection + centroid scan)", "bound": "hbm", "achieved": round(achieved, 1),
-                    "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                    "traffic": NCU_TRAFFIC_PER_LAYER, "peak_source": peak_src, "bytes_per_launch": int(bpl),
-                    "launch_us": round(avg_ms * 1e3, 2), "launches_timed": len(scan_ms),
-                    "timed_span": "projection + centroid scan (the scan is launched as a programmatic "
-                                  "dependent of the projection and streams keys while it runs)"}
-    path_gbs = path_bytes / (ms_per_step / 1e3) / 1e9
+    # Roofline of the unit the step is made of: one layer's lookup chain (k_project_mma ->
+    # k_search_decode -> k_combine, chained by programmatic dependent launch), its duration
+    # the timed step divided by the layers, its bytes the layer's algorithmic bytes.
+    layer_s = ms_per_step / CFG["layers"] / 1e3
+    traffic, traffic_src = ncu_traffic()
+    roofline = hbm_roofline("per-layer alut_lookup_combine chain: k_project_mma -> k_search_decode -> k_combine "
+                            "(programmatic dependent launch)", path_bytes / CFG["layers"], layer_s, peaks,
+                            traffic=traffic, traffic_source=traffic_src, peak_source=peak_src,
+                            timing="timed 48-layer step / 48 (CUDA events over the timed region)",
+                            bytes_note="routed tables' keys + text basis + x + looked-up rows + output read/write")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -538,13 +864,27 @@ def run_alut(args, rank, world, local, device):
         cpu = {"value": round(v, 1), "unit": "lookups/s", "cores": cores, "kind": "port",
                "sample": f"CPU oracle (C restatement of the reference torch path) over layers 0-{CPU_LAYERS - 1} "
                          f"of the step, {n} passes in {secs:.1f} s"}
+    # Free the decode tables before the other workloads (config 4 alone holds 49 GB).
+    del step, e2e, engines, managers
+    gc.collect()
+    torch.cuda.empty_cache()
     workloads = None
     if not args.no_workloads:
         flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
         workloads = {}
         if world == 1:
-            workloads["c3_prefill_layer"] = c3_workload(args, device, flush, peaks)
-        workloads["c5_sharded_table"] = c5_workload(args, rank, world, device, flush, peaks)
+            workloads["c1_single_table"] = c1_workload(args, device, flush, peaks, checker)
+            workloads["c3_prefill_layer"] = c3_workload(args, device, flush, peaks, checker)
+            gc.collect()
+            torch.cuda.empty_cache()
+            workloads["c4_deepseek_prefill_decode"] = c4_workload(args, device, flush, peaks, checker)
+            gc.collect()
+            torch.cuda.empty_cache()
+        workloads["c5_sharded_table"] = c5_workload(args, rank, world, device, flush, peaks, checker)
+    parity = checker.summary()
+    if world > 1:
+        for k in ("checked", "mismatches", "exempt"):
+            parity[k] = sum_over_ranks(parity[k], world, device)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "lookups/s", "n_gpus": world,
@@ -553,13 +893,12 @@ def run_alut(args, rank, world, local, device):
             "data": "synthetic (seeded random tables and routing)", "config": config_dict(world),
             "lookups_per_step": total_lookups // args.steps,
             "e2e": {"value": round(total_lookups / (e2e_ms / 1e3), 1), "unit": "lookups/s",
-                    "h2d_bytes_per_step": e2e.h2d_bytes, "d2h_bytes_per_step": e2e.d2h_bytes,
+                    "h2d_bytes_per_step": e2e_io[0], "d2h_bytes_per_step": e2e_io[1],
                     "ms_per_step": round(e2e_ms / args.steps, 5)},
             "gpu_launches": KERNELS_PER_LAYER * CFG["layers"] * args.steps,
             "roofline": roofline,
-            "path_roofline": {"bytes_per_step": path_bytes, "achieved_gbs": round(path_gbs, 1),
-                              "frac": round(path_gbs / peaks["hbm_gbs"], 4), "peak_source": peak_src},
             "cpu_baseline": cpu,
+            "parity": parity,
             "clocks": clocks.summary(),
             "workloads": workloads,
         }
