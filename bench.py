@@ -651,6 +651,71 @@ def c5_workload(args, rank, world, device, flush, peaks, checker):
     }
 
 
+# ---- crossover sweep of the scan and projection choices -------------------------------------
+
+CROSSOVER_CASES = [  # name, tokens, top_k, experts, K, L, H, looked-up fraction, Zipf exponent
+    ("c1_single_table", 256, 1, 1, 256, 64, 2048, 1.0, None),
+    ("q64", 64, 8, 128, 1024, 64, 2048, 0.4, None),
+    ("q128", 128, 8, 128, 1024, 64, 2048, 0.4, None),
+    ("q256", 256, 8, 128, 1024, 64, 2048, 0.4, None),
+    ("q512", 512, 8, 128, 1024, 64, 2048, 0.4, None),
+    ("q1024_zipf", 1024, 8, 128, 1024, 64, 2048, 0.4, 1.1),
+    ("c3_prefill", 4096, 8, 128, 1024, 64, 2048, 0.4, 1.1),
+    ("c4_prefill_layer", 2048, 6, 72, 2048, 96, 2560, 0.4, None),
+    ("one_table_4k", 4096, 1, 1, 4096, 128, 1024, 1.0, None),
+]
+
+
+def crossover(args, device, flush):
+    """Median device time of one lookup (graph replay, L2 flushed) per batch shape, with the
+    scan the library picks for it. Builds of the library with other thresholds
+    (-DALUT_TC_MIN_PAIRS, -DALUT_TC_MIN_SLOTS_PER_TABLE, -DALUT_PT_MIN_TOKENS), selected
+    with TABLEMOE_ALUT_LIB, give the other side of each choice."""
+    from table_moe.cache_engine import HybridStorageManager, VectorSearchEngine, _alut
+    from table_moe.cache_engine.step_graph import LookupStepGraph
+
+    reread = torch.ones(64 << 20, dtype=torch.float32, device=device)
+    lib = _alut.load()
+    out = {}
+    for name, q, s, e, k, l, h, frac, zipf in CROSSOVER_CASES:
+        g = torch.Generator(device=device).manual_seed(1)
+        raw = torch.randn(e, 2, k, l, generator=g, device=device)
+        values = torch.randn(e, 2, k, h, generator=g, device=device, dtype=torch.bfloat16).mul_(0.05)
+        pca = {m: {"proj": orthonormal_basis(h, l, g, device), "bias": torch.zeros(l, device=device)}
+               for m in ("vision", "text")}
+        mgr = HybridStorageManager.from_tables(0, raw, values, pca, keys=raw, enable_online=False)
+        logits = torch.randn(q, e, generator=g, device=device)
+        if zipf:
+            prior = torch.arange(1, e + 1, dtype=torch.float32, device=device) ** (-zipf)
+            logits = prior.log() - torch.log(-torch.log(torch.rand(q, e, generator=g, device=device)))
+        w, sel = torch.topk(torch.softmax(logits, -1), s, dim=-1)
+        reuse = torch.rand(q, s, generator=g, device=device) < frac
+        gr = LookupStepGraph([VectorSearchEngine(mgr)], q, s, variant="prefill_dot", renorm="to_one")
+        b = gr.layers[0]
+        for n2, t in (("x", torch.randn(q, h, generator=g, device=device)), ("sel", sel), ("reuse", reuse),
+                      ("weights", w), ("compute", ~reuse)):
+            getattr(b, n2).copy_(t)
+        gr.capture()
+        for _ in range(5):
+            gr.replay()
+        ts = []
+        for _ in range(30):
+            flush.fill_(1)
+            reread.sum()  # leaves L2 clean: the flush's dirty lines are written back here
+            a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            gr.replay()
+            c.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(c) * 1e3)
+        kind = lib.alut_scan_kind(mgr.alut_tables(), q, s)
+        out[name] = {"us": round(sorted(ts)[len(ts) // 2], 1),
+                     "scan": {0: "decode", 1: "cuda-core", 2: "tensor-core"}.get(kind, kind)}
+        del gr, mgr, raw, values
+        torch.cuda.empty_cache()
+    return out
+
+
 # ---- CPU arms: the oracle (test infrastructure) timed as the baseline -----------------
 
 def cpu_sample(managers, inputs):
@@ -736,7 +801,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--wl-steps", type=int, default=10, help="timed steps of each secondary workload")
     ap.add_argument("--no-workloads", action="store_true", help="skip the config 1/3/4/5 measurements")
-    ap.add_argument("--only", choices=["c1", "c3", "c4", "c5"], default=None,
+    ap.add_argument("--only", choices=["c1", "c3", "c4", "c5", "crossover"], default=None,
                     help="run only that secondary workload and print its JSON (profiling captures)")
     ap.add_argument("--layers", type=int, default=CFG["layers"],
                     help="fewer layers for profiling captures only (the benchmark is 48)")
@@ -758,6 +823,9 @@ def main():
             peaks, _ = measured_peaks()
             flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
             checker = Checker()
+            if args.only == "crossover":
+                print(json.dumps({"workload": "crossover", "cases": crossover(args, device, flush)}), flush=True)
+                return
             fn = {"c1": c1_workload, "c3": c3_workload, "c4": c4_workload}.get(args.only)
             res = fn(args, device, flush, peaks, checker) if fn else \
                 c5_workload(args, rank, world, device, flush, peaks, checker)

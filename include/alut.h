@@ -140,6 +140,16 @@ typedef struct alut_search_params {
  * Returns 0 on invalid arguments. */
 size_t alut_workspace_size(const alut_tables_t* tables, int32_t q, int32_t s);
 
+/* Which centroid scan a batch of q tokens x s slots takes on these tables (contiguous,
+ * 16-byte aligned key rows assumed): the decode chain (<= 32 tokens and <= 256 slots),
+ * the tensor-core scan (fp32 keys with L % 16 == 0, L <= 128, >= 512 slots and >= 12
+ * slots per routed table on average; it needs the key form of alut_prepare_keys) or the
+ * CUDA-core scans. Negative status on invalid arguments. */
+#define ALUT_SCAN_DECODE 0
+#define ALUT_SCAN_CUDA_CORE 1
+#define ALUT_SCAN_TENSOR_CORE 2
+int alut_scan_kind(const alut_tables_t* tables, int32_t q, int32_t s);
+
 /* Bytes of the split basis of these tables (0 if the tables do not qualify: fp32 proj,
  * H % 16 == 0, L % 8 == 0); includes the operand-order copy when the shape allows it. */
 size_t alut_basis_split_bytes(const alut_tables_t* tables);

@@ -353,7 +353,7 @@ static int launch_plan(const ProjPlanArgs& a, int* tabs, cudaStream_t st) {
     k_plan_scatter<<<grid, 256, 0, st>>>(a, tabs + ntab);
     return check_launch("k_plan_scatter");
   }
-  const size_t smem = plan_smem_bytes(2 * a.num_experts);
+  const size_t smem = plan_smem_bytes(2 * a.num_experts, pairs);
   int rc = allow_smem(reinterpret_cast<const void*>(k_plan), smem);
   if (rc) return rc;
   k_plan<<<1, kProjThreads, smem, st>>>(a);
@@ -540,7 +540,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
   // queries: tensor-core scan (tcgen05).
   const void* ksplit = keys == t->raw_keys ? t->raw_keys_split : t->keys_split;
   const Workspace wt = workspace_layout(b->q, b->s, t->l, 2 * t->num_experts, true);
-  if (ksplit && tc_tables_ok(t) && vec && pairs >= kTcMinPairs && ws_bytes >= wt.total) {
+  if (ksplit && tc_tables_ok(t) && vec && tc_scan_wanted(pairs, 2 * t->num_experts) && ws_bytes >= wt.total) {
     a.group = kTcRows;
     int rc = launch_plan(a, reinterpret_cast<int*>(base + w.tabs), st);
     if (rc) return rc;
@@ -588,6 +588,12 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     if (rc) return rc;
     if (g_prof_start && g_prof_stop && record_profile(g_prof_stop, st)) return ALUT_ECUDA;
     return ALUT_OK;
+  }
+  {
+    // Few tiles with full groups: smaller groups spread the scan over more SMs (each group
+    // reads its table chunk again, from L2).
+    const int64_t est_tiles = (static_cast<int64_t>(pairs) + kSearchGroup - 1) / kSearchGroup * ceil_div(t->k, kSearchChunkK);
+    a.group = est_tiles < num_sms() ? kCcSmallGroup : kSearchGroup;
   }
   int rc = launch_plan(a, reinterpret_cast<int*>(base + w.tabs), st);
   if (rc) return rc;
@@ -964,9 +970,19 @@ int alut_prepare_basis(const alut_tables_t* t, void* out, size_t out_bytes, alut
   return check_launch("k_split_basis_tc");
 }
 
+int alut_scan_kind(const alut_tables_t* t, int32_t q, int32_t s) {
+  if (!t || q < 0 || s < 0 || t->l <= 0 || t->num_experts <= 0) return fail(ALUT_EINVAL, "scan_kind: arguments");
+  const int64_t slots = static_cast<int64_t>(q) * s;
+  if (tc_tables_ok(t) && tc_scan_wanted(slots, 2 * t->num_experts)) return ALUT_SCAN_TENSOR_CORE;
+  const int esz = dtype_size(t->key_dtype);
+  if (t->l % 8 == 0 && static_cast<int64_t>(t->l) * esz <= 512 && q <= kDecodeMaxTokens && slots <= kDecodeMaxPairs)
+    return ALUT_SCAN_DECODE;
+  return ALUT_SCAN_CUDA_CORE;
+}
+
 size_t alut_workspace_size(const alut_tables_t* tables, int32_t q, int32_t s) {
   if (!tables || q < 0 || s < 0 || tables->l <= 0 || tables->num_experts <= 0) return 0;
-  const bool tc = tc_tables_ok(tables) && static_cast<int64_t>(q) * s >= kTcMinPairs;
+  const bool tc = tc_tables_ok(tables) && tc_scan_wanted(static_cast<int64_t>(q) * s, 2 * tables->num_experts);
   return workspace_layout(q, s, tables->l, 2 * tables->num_experts, tc).total;
 }
 

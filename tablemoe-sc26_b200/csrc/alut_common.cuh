@@ -19,6 +19,9 @@ constexpr int kMaxL = 256;               // L <= kMaxL (outputs per projection t
 constexpr int kSearchThreads = 128;      // one centroid per thread
 constexpr int kSearchChunkK = kSearchThreads;
 constexpr int kSearchGroup = 32;         // (token, slot) pairs scored per search tile
+// Slots per search group of the CUDA-core scans of large batches: kSearchGroup, or
+// kCcSmallGroup when the batch would otherwise give fewer (group, chunk) tiles than SMs.
+constexpr int kCcSmallGroup = 8;
 constexpr int kMaxTables = 4096;         // 2 * num_experts
 constexpr int kMaxSlots = 64;            // top_k
 constexpr int kCombineThreads = 64;      // 8 elements per thread -> 512 per CTA
@@ -246,7 +249,7 @@ inline int proj_splits(int q, int h) {
 inline Workspace workspace_layout(int q, int s, int l, int num_tables, bool tc = false) {
   Workspace w{};
   const int64_t pairs = static_cast<int64_t>(q) * s;
-  w.max_groups = (pairs + kSearchGroup - 1) / kSearchGroup + (pairs < num_tables ? pairs : num_tables) + 1;
+  w.max_groups = (pairs + kCcSmallGroup - 1) / kCcSmallGroup + (pairs < num_tables ? pairs : num_tables) + 1;
   size_t off = 0;
   w.meta = off;     off = align256(off + sizeof(int32_t) * 8);
   w.qlow = off;     off = align256(off + sizeof(float) * (static_cast<int64_t>(q) * l + 8));

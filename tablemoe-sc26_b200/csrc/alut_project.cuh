@@ -78,7 +78,9 @@ __host__ __device__ inline ProjSmem proj_smem_layout(int l) {
   return s;
 }
 inline size_t proj_smem_bytes(int l) { return proj_smem_layout(l).total; }
-inline size_t plan_smem_bytes(int num_tables) { return sizeof(int) * 3 * num_tables; }
+inline size_t plan_smem_bytes(int num_tables, int64_t pairs) {
+  return sizeof(int) * (3 * static_cast<size_t>(num_tables) + static_cast<size_t>(pairs));
+}
 
 // ---- planning (large batches) --------------------------------------------------------------
 
@@ -99,6 +101,20 @@ __device__ __forceinline__ int block_exclusive_scan_256(int v, int* scratch, int
   return incl - v;
 }
 
+// Table of slot p, or -1 when the slot is not searched (reuse mask off) or its expert id is
+// out of range (then *bad is set).
+__device__ __forceinline__ int plan_table(const ProjPlanArgs& a, int64_t p, bool* bad) {
+  const int qq = static_cast<int>(p / a.s), ss = static_cast<int>(p % a.s);
+  const bool r = a.reuse ? (a.reuse[qq * a.reuse_stride + ss] != 0) : true;
+  if (!r) return -1;
+  const int64_t e = a.sel[qq * a.sel_stride + ss];
+  if (e < 0 || e >= a.num_experts) {
+    *bad = true;
+    return -1;
+  }
+  return static_cast<int>(e) * 2 + (a.is_vision[qq] ? 0 : 1);
+}
+
 // Bucket the searched pairs by table (one CTA of kProjThreads threads): per-table counts,
 // block scans, group list (<= kSearchGroup pairs of one table each), scatter of pair ids.
 __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
@@ -106,25 +122,27 @@ __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
   const int tid = threadIdx.x;
   const int G = a.group > 0 ? a.group : kSearchGroup;
   const int ntab = 2 * a.num_experts;
-  const int64_t pairs = static_cast<int64_t>(a.q) * a.s;
+  const int pairs = a.q * a.s;  // <= kPlanWideSlots (the caller picks the wide plan above)
   int* counts = plan_smem;
   int* offs = plan_smem + ntab;
+  int* tab_of = plan_smem + 3 * ntab;  // table of each slot, -1 when not searched
   __shared__ int scan_scratch[kProjThreads];
   __shared__ int s_tot_c, s_tot_g;
 
   for (int t = tid; t < ntab; t += kProjThreads) counts[t] = 0;
-  __syncthreads();
-  for (int64_t p = tid; p < pairs; p += kProjThreads) {
-    const int qq = static_cast<int>(p / a.s), ss = static_cast<int>(p % a.s);
+  // Every slot's routing is read once, in independent loads (no atomics in this loop, so
+  // the loads of successive slots overlap), into shared memory.
+  bool bad = false;
+#pragma unroll 4
+  for (int p = tid; p < pairs; p += kProjThreads) {
+    tab_of[p] = plan_table(a, p, &bad);
     a.best[p] = 0ull;
-    const bool r = a.reuse ? (a.reuse[qq * a.reuse_stride + ss] != 0) : true;
-    if (!r) continue;
-    const int64_t e = a.sel[qq * a.sel_stride + ss];
-    if (e < 0 || e >= a.num_experts) {
-      atomicOr(&a.meta[1], kErrBadExpert);
-      continue;
-    }
-    atomicAdd(&counts[static_cast<int>(e) * 2 + (a.is_vision[qq] ? 0 : 1)], 1);
+  }
+  if (bad) atomicOr(&a.meta[1], kErrBadExpert);
+  __syncthreads();
+  for (int p = tid; p < pairs; p += kProjThreads) {
+    const int t = tab_of[p];
+    if (t >= 0) atomicAdd(&counts[t], 1);
   }
   __syncthreads();
   const int per = (ntab + kProjThreads - 1) / kProjThreads;
@@ -147,16 +165,13 @@ __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
   }
   if (tid == 0) a.meta[0] = s_tot_g;
   __syncthreads();
-  // Scatter pair ids into their table's bucket (the order inside a bucket does not
-  // matter: every pair's result is independent of the others).
-  for (int64_t p = tid; p < pairs; p += kProjThreads) {
-    const int qq = static_cast<int>(p / a.s), ss = static_cast<int>(p % a.s);
-    const bool r = a.reuse ? (a.reuse[qq * a.reuse_stride + ss] != 0) : true;
-    if (!r) continue;
-    const int64_t e = a.sel[qq * a.sel_stride + ss];
-    if (e < 0 || e >= a.num_experts) continue;
-    const int pos = atomicAdd(&offs[static_cast<int>(e) * 2 + (a.is_vision[qq] ? 0 : 1)], 1);
-    a.sorted[pos] = static_cast<int>(p);
+  // Scatter slot ids into their table's bucket (the order inside a bucket does not matter:
+  // every slot's result is independent of the others).
+  for (int p = tid; p < pairs; p += kProjThreads) {
+    const int t = tab_of[p];
+    if (t < 0) continue;
+    const int pos = atomicAdd(&offs[t], 1);
+    a.sorted[pos] = p;
   }
 }
 
@@ -168,20 +183,6 @@ __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
 // (3) k_plan_scatter: writes each searched slot id into its table's bucket (warp-aggregated
 //     atomics on the bucket cursors). The order inside a bucket does not matter.
 // `counts` must be zero before (1).
-
-// Table of slot p, or -1 when the slot is not searched (reuse mask off) or its expert id is
-// out of range (then *bad is set).
-__device__ __forceinline__ int plan_table(const ProjPlanArgs& a, int64_t p, bool* bad) {
-  const int qq = static_cast<int>(p / a.s), ss = static_cast<int>(p % a.s);
-  const bool r = a.reuse ? (a.reuse[qq * a.reuse_stride + ss] != 0) : true;
-  if (!r) return -1;
-  const int64_t e = a.sel[qq * a.sel_stride + ss];
-  if (e < 0 || e >= a.num_experts) {
-    *bad = true;
-    return -1;
-  }
-  return static_cast<int>(e) * 2 + (a.is_vision[qq] ? 0 : 1);
-}
 
 __global__ void __launch_bounds__(256) k_plan_count(ProjPlanArgs a, int* counts) {
   extern __shared__ __align__(16) int hist[];
@@ -628,14 +629,17 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   for (int i = tid; i < 2 * L; i += kProjThreads)
     s_bias[i / L][i % L] = static_cast<const float*>(a.bias[i / L])[i % L];
   const int kn16 = (k_end - k_begin) * 16;  // elements of k in this slice
-  if (lay.staged) {
-    const int units = kn16 / 8;  // 16-byte units per slice row
-    for (int i = tid; i < 6 * L * units; i += kProjThreads) {
-      const int row = i / units, u = i % units;  // row = (m*3 + part)*L + col
+  // The text basis is staged before the dependency wait (text is every decode token's
+  // modality); the vision basis after it, only when the tile holds a vision token.
+  const int units = kn16 / 8;  // 16-byte units per slice row
+  auto stage_modality = [&](int m) {
+    for (int i = tid; i < 3 * L * units; i += kProjThreads) {
+      const int row = m * 3 * L + i / units, u = i % units;  // row = (m*3 + part)*L + col
       cp_async16(psm + static_cast<size_t>(row) * lay.pitch + u * 16,
                  a.proj_split + static_cast<int64_t>(row) * H + static_cast<int64_t>(k_begin) * 16 + u * 8);
     }
-  }
+  };
+  if (lay.staged) stage_modality(1);
   cp_async_commit();
   pdl_wait();
   // This call's inputs, requested together: the first k-block of this thread's x fragments
@@ -666,6 +670,10 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   const bool need_m[2] = {vis_bits != 0u, (rows_bits & ~vis_bits) != 0u};
   const int m_r0 = (vis_bits >> gq) & 1u ? 0 : 1, m_r1 = (vis_bits >> (gq + 8)) & 1u ? 0 : 1;
   if (warp == 0 && lane < kProjTileQ) mod[lane] = lane_vis ? 0 : 1;  // for finish_rows
+  if (lay.staged && need_m[0]) {  // uniform over the CTA: every warp saw the same ballot
+    stage_modality(0);
+    cp_async_commit();
+  }
   if (a.zero_best && blockIdx.x == 0)
     for (int i = tid; i < a.zero_n; i += kProjThreads) a.zero_best[i] = 0ull;
   cp_async_wait<0>();

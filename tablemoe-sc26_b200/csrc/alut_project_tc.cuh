@@ -39,7 +39,10 @@ namespace alut {
 constexpr int kPtKc = 64;          // K (H) columns per pipeline stage
 constexpr int kPtThreads = 288;    // warps 0-3 epilogue, 4 copies, 8 MMA (5-7 idle)
 constexpr int kPtMaxStages = 6;
-constexpr int kPtMinTokens = 256;  // below this the decode-shaped projections are used
+#ifndef ALUT_PT_MIN_TOKENS
+#define ALUT_PT_MIN_TOKENS 1024
+#endif
+constexpr int kPtMinTokens = ALUT_PT_MIN_TOKENS;  // below this the decode-shaped projections are used
 constexpr size_t kPtSmemBudget = 200 * 1024;
 
 inline bool pt_shape_ok(int l, int h) { return l > 0 && l % 16 == 0 && l <= kTcMaxL && h > 0 && h % kPtKc == 0; }

@@ -43,7 +43,21 @@ constexpr int kTcMaxL = 128;
 constexpr int kTcEpiThreads = 256;  // warps 0-7: (TMEM lane quarter, column half)
 constexpr int kTcThreads = 320;     // + producer warp 8 + MMA warp 9
 constexpr int kTcProducerWarp = 8, kTcMmaWarp = 9;
-constexpr int kTcMinPairs = 512;    // below this the CUDA-core scans are used
+#ifndef ALUT_TC_MIN_PAIRS
+#define ALUT_TC_MIN_PAIRS 512
+#endif
+constexpr int kTcMinPairs = ALUT_TC_MIN_PAIRS;  // below this the CUDA-core scans are used
+// ... and below this many slots per routed table on average (slots / min(tables, slots)):
+// a 128 x 128 MMA tile whose group holds a few slots wastes the tensor cores, and the
+// CUDA-core scans are faster there (measured on B200: 64 tokens x top-8 over 128 experts).
+#ifndef ALUT_TC_MIN_SLOTS_PER_TABLE
+#define ALUT_TC_MIN_SLOTS_PER_TABLE 12
+#endif
+constexpr int kTcMinSlotsPerTable = ALUT_TC_MIN_SLOTS_PER_TABLE;
+inline bool tc_scan_wanted(int64_t slots, int num_tables) {
+  const int64_t tables = slots < num_tables ? slots : num_tables;
+  return slots >= kTcMinPairs && slots >= kTcMinSlotsPerTable * tables;
+}
 constexpr int kTcCand = 8;          // candidate list per (slot, column half)
 constexpr int kTcMaxStages = 8;
 constexpr int kTcAcc = 4;                          // fp32 128x128 accumulators in TMEM

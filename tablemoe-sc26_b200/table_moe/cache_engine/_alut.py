@@ -24,6 +24,7 @@ KEYS_NORMALISED, KEYS_RAW = 0, 1
 RENORM_NONE, RENORM_TO_ONE, RENORM_TO_ROWSUM = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 2 << 20  # ALUT_NOALLOC_SCRATCH_BYTES
 PEER_HANDLE_BYTES = 64  # ALUT_PEER_HANDLE_BYTES
+SCAN_DECODE, SCAN_CUDA_CORE, SCAN_TENSOR_CORE = 0, 1, 2  # alut_scan_kind
 ERR_BAD_EXPERT, ERR_COPY_TIMEOUT, ERR_MMA_TIMEOUT = 1, 4, 8  # ALUT_ERR_* device error bits
 
 _DTYPE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
@@ -69,6 +70,7 @@ _PP = ctypes.POINTER(SearchParams)
 
 SIGNATURES = {
     "alut_workspace_size": (_SZ, [_TP, _I32, _I32]),
+    "alut_scan_kind": (ctypes.c_int, [_TP, _I32, _I32]),
     "alut_basis_split_bytes": (_SZ, [_TP]),
     "alut_keys_split_bytes": (_SZ, [_TP]),
     "alut_prepare_keys": (ctypes.c_int, [_TP, _I32, _P, _SZ, _P]),

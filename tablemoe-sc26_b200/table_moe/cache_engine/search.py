@@ -64,12 +64,17 @@ class VectorSearchEngine:
             }
         return self.search_dims_cache
 
-    # Batches of at least this many searched slots may use the tensor-core scan.
-    TENSOR_CORE_MIN_PAIRS = 512
+    def _tensor_core_wanted(self, bs, top_k):
+        """Whether the library will run the tensor-core scan for this batch shape (then the
+        manager prepares the key form once)."""
+        fn = getattr(self.manager, "alut_tables", None)
+        if fn is None or bs * top_k == 0:
+            return False
+        return self._lib.alut_scan_kind(fn(), bs, top_k) == _alut.SCAN_TENSOR_CORE
 
-    def _tables(self, with_values=False, pairs=0, keyset=None):
+    def _tables(self, with_values=False, shape=(0, 0), keyset=None):
         prep = getattr(self.manager, "prepare_tensor_core", None)
-        if prep is not None and keyset is not None and pairs >= self.TENSOR_CORE_MIN_PAIRS:
+        if prep is not None and keyset is not None and self._tensor_core_wanted(*shape):
             return prep(keyset)
         fn = getattr(self.manager, "alut_tables", None)
         if fn is not None:
@@ -140,7 +145,7 @@ class VectorSearchEngine:
             reuse = reuse.bool().contiguous()
         if out_hit.stride() != out_idx.stride() or out_hit.stride(-1) != 1:
             raise ValueError("out_hit / out_idx must share strides with unit inner stride")
-        tables = self._tables(pairs=bs * top_k, keyset=keyset)
+        tables = self._tables(shape=(bs, top_k), keyset=keyset)
         ws = self._scratch(tables, bs, top_k)
         batch = _alut.make_batch(x, sel, vis, reuse)
         params = _alut.make_params(keyset, normalize, cmp_ge, thr_vision, thr_text,
@@ -335,7 +340,7 @@ class VectorSearchEngine:
             reuse = reuse_mask
             if reuse is not None and (reuse.dtype != torch.bool or reuse.stride(-1) != 1):
                 reuse = reuse.bool().contiguous()
-            tables = self._tables(with_values=True, pairs=bs * top_k, keyset=keyset)
+            tables = self._tables(with_values=True, shape=(bs, top_k), keyset=keyset)
             ws = self._scratch(tables, bs, top_k)
             batch = _alut.make_batch(x, sel, vis, reuse)  # x, sel, vis, reuse stay referenced
             params = _alut.make_params(keyset, normalize, cmp_ge, tv, tt, CacheConfig.OFFLINE_COSINE_EPS)

@@ -221,14 +221,15 @@ def test_projection_matches_oracle():
 
 
 @pytest.mark.parametrize("Q,H,L,vis,normalize", [
-    (1000, 2048, 64, "mixed", False),    # tiles holding both modalities
+    (1100, 2048, 64, "mixed", False),    # tiles holding both modalities
     (4096, 2048, 64, "first1024", True),  # C3-like: image tokens first, pure tiles
-    (300, 512, 128, "mixed", True),      # ragged last tile, L = 128
-    (777, 256, 48, "none", False),       # L = 48, text only
+    (1300, 512, 128, "mixed", True),     # ragged last tile, L = 128
+    (1777, 256, 48, "none", False),      # L = 48, text only
+    (300, 512, 128, "mixed", True),      # below the tcgen05 cut: decode-shaped projection
     (12000, 256, 64, "mixed", False),    # 94 tiles: persistent CTAs, no H split
 ])
 def test_large_batch_projection_matches_oracle(Q, H, L, vis, normalize):
-    """bf16 tokens, fp32 basis, >= 256 tokens: the tcgen05 projection (128-token tiles, basis
+    """bf16 tokens, fp32 basis, >= 1024 tokens: the tcgen05 projection (128-token tiles, basis
     in three bf16 parts); q within fp32 accuracy of the oracle."""
     g = torch.Generator().manual_seed(Q + L)
     x = torch.randn(Q, H, generator=g).to(torch.bfloat16)

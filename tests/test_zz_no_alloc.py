@@ -46,7 +46,7 @@ def manager():
 def _run(lib, mgr, c, noalloc):
     Q, S = c["sel"].shape
     # Batches of >= 512 slots take the tensor-core scan when the key form is prepared.
-    tables = mgr.prepare_tensor_core(_alut.KEYS_RAW) if Q * S >= 512 else mgr.alut_tables()
+    tables = mgr.prepare_tensor_core(_alut.KEYS_RAW) if Q * S >= 768 else mgr.alut_tables()
     batch = _alut.make_batch(c["x"], c["sel"], c["vis"], c["reuse"])
     params = _alut.make_params(_alut.KEYS_RAW, False, False, 0.0, 0.0, 1e-6)
     out = torch.full((Q, mgr.hidden_dim), 7.0, dtype=torch.bfloat16, device=DEV)
@@ -65,10 +65,10 @@ def _run(lib, mgr, c, noalloc):
     return out, hit, idx
 
 
-@pytest.mark.parametrize("Q,S", [(16, 8), (64, 4), (256, 4)])
+@pytest.mark.parametrize("Q,S", [(16, 8), (64, 4), (512, 4)])
 def test_noalloc_matches_workspace_entry_on_consecutive_calls(manager, Q, S):
-    """(16, 8): decode chain; (64, 4): planned CUDA-core scan; (256, 4): 1024 searched-or-not
-    slots on tables with the tensor-core key form (tensor-core scan when its layout fits)."""
+    """(16, 8): decode chain; (64, 4): planned CUDA-core scan; (512, 4): 2048 slots over 64
+    tables with the tensor-core key form (tensor-core scan when its layout fits)."""
     lib = _alut.load()
     for seed in (1, 2):  # two calls in a row, different batches, the shared scratch reused
         c = _case(seed, Q=Q, S=S)
