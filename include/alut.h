@@ -216,6 +216,22 @@ int alut_lookup_combine(const alut_tables_t* tables, const alut_batch_t* batch,
                         int64_t* out_idx, int64_t out_stride_hit, void* workspace,
                         size_t workspace_bytes, alut_stream_t stream);
 
+/* alut_lookup_combine that also adds the computed experts' outputs, i.e. the whole combine
+ * of the MoE layer (cached_layers.py:452-465: collected[t, s] = expert output for computed
+ * slots, the looked-up value row for hit slots, then bmm with the renormalised weights):
+ *   out[t, :] (+)= sum_s w~[t, s] * (hit[t, s] ? value row : compute_mask[t, s] ?
+ *                                     computed[t, s, :] : 0)
+ * in slot order, fp32 arithmetic. computed: [Q, S, H] in the value dtype with element
+ * strides computed_stride_t (token) and computed_stride_s (slot); rows of non-computed
+ * slots are not read. compute_mask is required. */
+int alut_lookup_combine_experts(const alut_tables_t* tables, const alut_batch_t* batch,
+                                const alut_search_params_t* params, const float* weights, int64_t weight_stride,
+                                const uint8_t* compute_mask, int64_t compute_stride, const void* computed,
+                                int64_t computed_stride_t, int64_t computed_stride_s, int32_t renorm,
+                                int32_t accumulate, void* out, int64_t out_stride, int32_t out_dtype,
+                                uint8_t* out_hit, int64_t* out_idx, int64_t out_stride_hit, void* workspace,
+                                size_t workspace_bytes, alut_stream_t stream);
+
 /* Centroid-range shard: search a table slice whose row 0 is global centroid idx_offset
  * and write, per (token, slot), the packed best candidate
  *   (order-preserving bits of the score << 32) | (0xFFFFFFFF - global index)
@@ -333,6 +349,13 @@ int alut_route(int32_t q, int32_t num_experts, int32_t top_k, const void* logits
 int alut_keep_mask(int32_t q, int32_t num_experts, int32_t top_k, const int64_t* sel, const float* weights,
                    int64_t in_stride, const float* attn, double keep_rate, uint8_t* compute, uint8_t* reuse,
                    int64_t out_stride, void* workspace, size_t workspace_bytes, alut_stream_t stream);
+
+/* Load-time key normalisation (table_moe/cache_engine/manager.py:24-31, :205-207): for each
+ * of `rows` rows of l elements (dtype, row strides in elements; dst may equal src)
+ * dst = src / max(||src||, eps) computed in fp32, zero rows (||src|| <= eps) kept at zero,
+ * rounded to dtype. Makes keys_buffer from raw_keys_buffer on the device. */
+int alut_normalize_rows(int64_t rows, int32_t l, const void* src, int64_t src_stride, void* dst, int64_t dst_stride,
+                        int32_t dtype, float eps, alut_stream_t stream);
 
 /* Device-side error bits of a workspace (or, with workspace NULL, of the no-allocation
  * entry point's scratch). Kernels set them and never clear them, so they accumulate over

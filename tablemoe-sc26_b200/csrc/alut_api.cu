@@ -883,6 +883,32 @@ int alut_keep_mask(int32_t q, int32_t num_experts, int32_t top_k, const int64_t*
   return check_launch("k_route_keep");
 }
 
+int alut_normalize_rows(int64_t rows, int32_t l, const void* src, int64_t src_stride, void* dst, int64_t dst_stride,
+                        int32_t dtype, float eps, alut_stream_t stream) {
+  if (rows < 0 || l <= 0) return fail(ALUT_EINVAL, "normalize_rows: rows=%lld l=%d", static_cast<long long>(rows), l);
+  if (rows == 0) return ALUT_OK;
+  if (!src || !dst) return fail(ALUT_EINVAL, "normalize_rows: NULL argument");
+  if (!dtype_ok(dtype)) return fail(ALUT_EDTYPE, "normalize_rows: dtype");
+  if (src_stride < l || dst_stride < l) return fail(ALUT_ESHAPE, "normalize_rows: strides");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>((rows * 32 + 255) / 256);
+  switch (dtype) {
+    case ALUT_F32:
+      k_normalize_rows<float><<<grid, 256, 0, st>>>(rows, l, static_cast<const float*>(src), src_stride,
+                                                   static_cast<float*>(dst), dst_stride, eps);
+      break;
+    case ALUT_BF16:
+      k_normalize_rows<__nv_bfloat16><<<grid, 256, 0, st>>>(rows, l, static_cast<const __nv_bfloat16*>(src), src_stride,
+                                                           static_cast<__nv_bfloat16*>(dst), dst_stride, eps);
+      break;
+    case ALUT_F16:
+      k_normalize_rows<__half><<<grid, 256, 0, st>>>(rows, l, static_cast<const __half*>(src), src_stride,
+                                                    static_cast<__half*>(dst), dst_stride, eps);
+      break;
+  }
+  return check_launch("k_normalize_rows");
+}
+
 int alut_workspace_errors(void* workspace, size_t workspace_bytes, int32_t clear, uint32_t* bits,
                           alut_stream_t stream) {
   if (!bits) return fail(ALUT_EINVAL, "workspace_errors: bits is NULL");
@@ -1150,13 +1176,13 @@ int alut_combine(const alut_tables_t* tables, const alut_batch_t* batch, const u
                         c, grid, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int alut_lookup_combine(const alut_tables_t* tables, const alut_batch_t* batch,
-                        const alut_search_params_t* params, const float* weights,
-                        int64_t weight_stride, const uint8_t* compute_mask,
-                        int64_t compute_stride, int32_t renorm, int32_t accumulate, void* out,
-                        int64_t out_stride, int32_t out_dtype, uint8_t* out_hit,
-                        int64_t* out_idx, int64_t out_stride_hit, void* workspace,
-                        size_t workspace_bytes, alut_stream_t stream) {
+static int lookup_combine_impl(const alut_tables_t* tables, const alut_batch_t* batch,
+                               const alut_search_params_t* params, const float* weights, int64_t weight_stride,
+                               const uint8_t* compute_mask, int64_t compute_stride, const void* computed,
+                               int64_t computed_stride_t, int64_t computed_stride_s, int32_t renorm,
+                               int32_t accumulate, void* out, int64_t out_stride, int32_t out_dtype,
+                               uint8_t* out_hit, int64_t* out_idx, int64_t out_stride_hit, void* workspace,
+                               size_t workspace_bytes, alut_stream_t stream) {
   int rc = check_tables(tables, true);
   if (rc) return rc;
   if (!tables->values) return fail(ALUT_EINVAL, "tables: values is NULL");
@@ -1205,9 +1231,42 @@ int alut_lookup_combine(const alut_tables_t* tables, const alut_batch_t* batch,
   c.out_hit = out_hit;
   c.out_idx = out_idx;
   c.out_hit_stride = out_stride_hit;
+  c.computed = computed;
+  c.computed_stride_t = computed_stride_t;
+  c.computed_stride_s = computed_stride_s;
+  const int vsz = dtype_size(tables->value_dtype);
+  const bool vec = combine_vec(tables, out, out_stride, out_dtype) &&
+                   (!computed || (aligned16(computed) && (computed_stride_t * vsz) % 16 == 0 &&
+                                  (computed_stride_s * vsz) % 16 == 0));
   dim3 grid(batch->q, ceil_div(tables->h, kCombineSpan));
-  return launch_combine(tables->value_dtype, out_dtype, combine_vec(tables, out, out_stride, out_dtype),
-                        c, grid, st);
+  return launch_combine(tables->value_dtype, out_dtype, vec, c, grid, st);
+}
+
+int alut_lookup_combine(const alut_tables_t* tables, const alut_batch_t* batch,
+                        const alut_search_params_t* params, const float* weights,
+                        int64_t weight_stride, const uint8_t* compute_mask,
+                        int64_t compute_stride, int32_t renorm, int32_t accumulate, void* out,
+                        int64_t out_stride, int32_t out_dtype, uint8_t* out_hit,
+                        int64_t* out_idx, int64_t out_stride_hit, void* workspace,
+                        size_t workspace_bytes, alut_stream_t stream) {
+  return lookup_combine_impl(tables, batch, params, weights, weight_stride, compute_mask, compute_stride, nullptr, 0,
+                             0, renorm, accumulate, out, out_stride, out_dtype, out_hit, out_idx, out_stride_hit,
+                             workspace, workspace_bytes, stream);
+}
+
+int alut_lookup_combine_experts(const alut_tables_t* tables, const alut_batch_t* batch,
+                                const alut_search_params_t* params, const float* weights, int64_t weight_stride,
+                                const uint8_t* compute_mask, int64_t compute_stride, const void* computed,
+                                int64_t computed_stride_t, int64_t computed_stride_s, int32_t renorm,
+                                int32_t accumulate, void* out, int64_t out_stride, int32_t out_dtype,
+                                uint8_t* out_hit, int64_t* out_idx, int64_t out_stride_hit, void* workspace,
+                                size_t workspace_bytes, alut_stream_t stream) {
+  if (!computed || !compute_mask) return fail(ALUT_EINVAL, "lookup_combine_experts: computed/compute_mask is NULL");
+  if (batch && tables && (computed_stride_s < tables->h || computed_stride_t < computed_stride_s * batch->s))
+    return fail(ALUT_ESHAPE, "lookup_combine_experts: computed strides");
+  return lookup_combine_impl(tables, batch, params, weights, weight_stride, compute_mask, compute_stride, computed,
+                             computed_stride_t, computed_stride_s, renorm, accumulate, out, out_stride, out_dtype,
+                             out_hit, out_idx, out_stride_hit, workspace, workspace_bytes, stream);
 }
 
 int alut_search_packed(const alut_tables_t* tables, const alut_batch_t* batch,

@@ -36,6 +36,12 @@ struct CombineArgs {
   uint8_t* out_hit;
   int64_t* out_idx;
   int64_t out_hit_stride;
+  // Optional: the computed experts' outputs [Q, S, H] in the value dtype (the wrapper's
+  // collected_expert_outputs, cached_layers.py:455-465): computed slots then add
+  // w~ * computed[t, s, :] in slot order with the looked-up rows, so the call produces the
+  // whole MoE combine (the reference's bmm of the renormalised weights).
+  const void* computed;
+  int64_t computed_stride_t, computed_stride_s;
 };
 
 constexpr int kCombineSpan = kCombineThreads * 8;
@@ -46,9 +52,9 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
   __shared__ float s_w[kMaxSlots];
   __shared__ uint8_t s_surv[kMaxSlots];
   __shared__ uint8_t s_look[kMaxSlots];
-  __shared__ int64_t s_off[kMaxSlots];
+  __shared__ const TV* s_off[kMaxSlots];
   __shared__ float s_wl[kMaxSlots];
-  __shared__ int64_t s_offl[kMaxSlots];
+  __shared__ const TV* s_offl[kMaxSlots];
   __shared__ int s_n;
   const int tid = threadIdx.x;
   const int t = blockIdx.x;
@@ -93,10 +99,12 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
     }
     const bool comp = comp_;
     const bool look = hit && ev && idx >= 0 && idx < a.k;
+    const bool add_comp = comp && !look && a.computed != nullptr;  // a hit row wins (cached_layers.py:452)
     s_w[s] = w_;
     s_surv[s] = (comp || hit) ? 1 : 0;
-    s_look[s] = look ? 1 : 0;
-    s_off[s] = look ? (e * a.vs_e + m * a.vs_m + idx * a.vs_k) : 0;
+    s_look[s] = (look || add_comp) ? 1 : 0;
+    s_off[s] = add_comp ? static_cast<const TV*>(a.computed) + t * a.computed_stride_t + s * a.computed_stride_s
+                        : static_cast<const TV*>(a.values) + (look ? (e * a.vs_e + m * a.vs_m + idx * a.vs_k) : 0);
   }
   __syncthreads();
   if (tid == 0) {
@@ -124,7 +132,6 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
   const int64_t h0 = static_cast<int64_t>(blockIdx.y) * kCombineSpan + tid * 8;
   if (h0 >= a.h) return;
   TO* out = static_cast<TO*>(a.out) + static_cast<int64_t>(t) * a.out_stride + h0;
-  const TV* vals = static_cast<const TV*>(a.values);
   float acc[8];
   if (kVec) {
     if (a.accumulate) load8_rw<TO>(out, acc);
@@ -137,7 +144,7 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
     for (; i + 4 <= n; i += 4) {
       float v[4][8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) load8<TV>(vals + s_offl[i + u] + h0, v[u]);
+      for (int u = 0; u < 4; ++u) load8<TV>(s_offl[i + u] + h0, v[u]);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const float w = s_wl[i + u];
@@ -147,7 +154,7 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
     }
     for (; i < n; ++i) {
       float v[8];
-      load8<TV>(vals + s_offl[i] + h0, v);
+      load8<TV>(s_offl[i] + h0, v);
       const float w = s_wl[i];
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = fmaf(w, v[j], acc[j]);
@@ -160,7 +167,7 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
     for (int j = 0; j < cnt; ++j) acc[j] = a.accumulate ? to_f32<TO>(out[j]) : 0.f;
     for (int i = 0; i < n; ++i) {
       const float w = s_wl[i];
-      for (int j = 0; j < cnt; ++j) acc[j] = fmaf(w, to_f32<TV>(vals[s_offl[i] + h0 + j]), acc[j]);
+      for (int j = 0; j < cnt; ++j) acc[j] = fmaf(w, to_f32<TV>(s_offl[i][h0 + j]), acc[j]);
     }
     for (int j = 0; j < cnt; ++j) out[j] = from_f32<TO>(acc[j]);
   }
@@ -202,6 +209,30 @@ __global__ void k_gather_rows(GatherArgs a) {
       dst[b] = ok ? src[b] : 0;
     }
   }
+}
+
+// Load-time key normalisation (manager.py:24-31 _normalize_last_dim, applied at :205-207):
+// y = x / max(||x||, eps) in fp32, rows with ||x|| <= eps set to zero, rounded to the table
+// dtype. One warp per row.
+template <typename T>
+__global__ void k_normalize_rows(int64_t rows, int l, const T* src, int64_t src_stride, T* dst, int64_t dst_stride,
+                                 float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (r >= rows) return;
+  const T* x = src + r * src_stride;
+  float ss = 0.f;
+  for (int c = lane; c < l; c += 32) {
+    const float v = to_f32<T>(x[c]);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float n = sqrtf(ss);
+  const float denom = fmaxf(n, eps);
+  const bool zero = n <= eps;
+  T* y = dst + r * dst_stride;
+  for (int c = lane; c < l; c += 32) y[c] = from_f32<T>(zero ? 0.f : to_f32<T>(x[c]) / denom);
 }
 
 }  // namespace alut

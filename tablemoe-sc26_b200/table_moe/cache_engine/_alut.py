@@ -82,6 +82,8 @@ SIGNATURES = {
                                     _I64, _I32, _P]),
     "alut_lookup_combine": (ctypes.c_int, [_TP, _BP, _PP, _P, _I64, _P, _I64, _I32, _I32, _P, _I64,
                                            _I32, _P, _P, _I64, _P, _SZ, _P]),
+    "alut_lookup_combine_experts": (ctypes.c_int, [_TP, _BP, _PP, _P, _I64, _P, _I64, _P, _I64, _I64, _I32, _I32,
+                                                   _P, _I64, _I32, _P, _P, _I64, _P, _SZ, _P]),
     "alut_lookup_combine_noalloc": (ctypes.c_int, [_TP, _BP, _PP, _P, _I64, _P, _I64, _I32, _I32, _P, _I64,
                                                    _I32, _P, _P, _I64, _P]),
     "alut_search_packed": (ctypes.c_int, [_TP, _BP, _PP, _P, _I64, _P, _P, _SZ, _P]),
@@ -98,6 +100,7 @@ SIGNATURES = {
                                   _P, _I64, _P, _SZ, _P]),
     "alut_keep_mask": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _I64, _P, ctypes.c_double, _P, _P, _I64, _P, _SZ,
                                       _P]),
+    "alut_normalize_rows": (ctypes.c_int, [_I64, _I32, _P, _I64, _P, _I64, _I32, ctypes.c_float, _P]),
     "alut_workspace_errors": (ctypes.c_int, [_P, _SZ, _I32, ctypes.POINTER(ctypes.c_uint32), _P]),
     "alut_set_profile_events": (ctypes.c_int, [_P, _P]),
     "alut_last_error": (ctypes.c_char_p, []),

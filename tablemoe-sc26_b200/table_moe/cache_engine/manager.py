@@ -34,7 +34,20 @@ def _resolve_cache_dtype():
 
 def normalize_rows(x: torch.Tensor, eps: float) -> torch.Tensor:
     """L2-normalise the last dim in fp32 with zero rows kept at zero, then cast back
-    (load-time key normalisation, manager.py:24-31)."""
+    (load-time key normalisation, manager.py:24-31). CUDA tensors go through the
+    ``alut_normalize_rows`` kernel; host tensors (fixtures, host-side preparation) through
+    the same arithmetic in torch."""
+    if x.is_cuda:
+        src = x.contiguous()
+        out = torch.empty_like(src)
+        rows = src.numel() // src.shape[-1] if src.numel() else 0
+        if rows:
+            l = src.shape[-1]
+            rc = _alut.load().alut_normalize_rows(rows, l, src.data_ptr(), l, out.data_ptr(), l,
+                                                  _alut.dtype_code(src.dtype), float(eps),
+                                                  _alut.stream_ptr(src.device))
+            _alut.check(rc, "alut_normalize_rows")
+        return out
     xf = x.float()
     n = torch.linalg.vector_norm(xf, dim=-1, keepdim=True)
     out = torch.where(n <= eps, torch.zeros_like(xf), xf / n.clamp_min(eps))
@@ -218,9 +231,14 @@ class HybridStorageManager:
         return pca
 
     def _load_cache_data(self):
-        """``L{layer}_E{e}_{mod}_cache.pt`` = {key [k,L], value [k,H]}, rows beyond k stay 0."""
+        """``L{layer}_E{e}_{mod}_cache.pt`` = {key [k,L], value [k,H]}, rows beyond k stay 0;
+        the normalised key set is made from the raw one on the device after all files."""
         root = os.path.join(CacheConfig.CACHE_DIR, f"layer_{self.layer_idx}")
         eps = float(CacheConfig.OFFLINE_COSINE_EPS)
+        self._load_files(root)
+        self.keys_buffer.copy_(normalize_rows(self.raw_keys_buffer, eps))
+
+    def _load_files(self, root):
         for path in glob.glob(os.path.join(root, "*_cache.pt")):
             try:
                 parts = os.path.basename(path)[:-3].split("_")
@@ -232,7 +250,6 @@ class HybridStorageManager:
                 keys = data["key"].to(dtype=self.dtype)
                 k = keys.shape[0]
                 self.raw_keys_buffer[eid, mid, :k] = keys.to(self.device)
-                self.keys_buffer[eid, mid, :k] = normalize_rows(keys, eps).to(self.device)
                 self.values_buffer[eid, mid, :k] = data["value"].to(dtype=self.dtype, device=self.device)
             except Exception as exc:  # same policy as the reference: log and skip the file
                 print(f"Error loading {path}: {exc}")

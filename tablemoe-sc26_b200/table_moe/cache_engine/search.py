@@ -294,7 +294,7 @@ class VectorSearchEngine:
     # ---- fused lookup (search + gather + weighted accumulate) --------------------------
     def lookup_combine(self, hidden_states, selected_experts, is_vision_mask, reuse_mask, routing_weights,
                        *, compute_mask=None, out=None, variant="prefill_dot", renorm="to_one",
-                       return_hits=False, hit_out=None, idx_out=None):
+                       return_hits=False, hit_out=None, idx_out=None, computed=None):
         """Search every reuse slot, then out[t] (+)= sum over hits of w~[t,s] * value row.
 
         ``variant`` picks the search semantics of one of the methods above ("prefill",
@@ -303,7 +303,10 @@ class VectorSearchEngine:
         deepseek_layers.py:715-727). ``out`` (accumulated into when given) defaults to a
         new [bs, H] tensor of the value dtype. ``hit_out`` / ``idx_out`` ([bs, top_k] bool /
         int64, unit inner stride, shared strides) receive the hits and indices in place;
-        ``return_hits`` allocates them instead.
+        ``return_hits`` allocates them instead. ``computed`` ([bs, top_k, H] in the value
+        dtype, the wrapper's collected expert outputs) adds the computed slots' outputs with
+        the same renormalised weights, making the call the layer's whole combine
+        (cached_layers.py:452-465); it needs ``compute_mask``.
         """
         rules = {
             "prefill": (_alut.KEYS_NORMALISED, True, True, CacheConfig.OFFLINE_COSINE_THRESHOLD_VISION,
@@ -344,13 +347,26 @@ class VectorSearchEngine:
             ws = self._scratch(tables, bs, top_k)
             batch = _alut.make_batch(x, sel, vis, reuse)  # x, sel, vis, reuse stay referenced
             params = _alut.make_params(keyset, normalize, cmp_ge, tv, tt, CacheConfig.OFFLINE_COSINE_EPS)
-            rc = self._lib.alut_lookup_combine(
-                tables, batch, params, w.data_ptr(), w.stride(0), _alut.ptr(comp),
-                0 if comp is None else comp.stride(0), rn, int(accumulate), out.data_ptr(), out.stride(0),
-                _alut.dtype_code(out.dtype), _alut.ptr(hit), _alut.ptr(idx), top_k if hit is None else hit.stride(0),
-                ws.data_ptr(),
-                ws.numel(), _alut.stream_ptr(self.device))
-            _alut.check(rc, "alut_lookup_combine")
+            hs = top_k if hit is None else hit.stride(0)
+            if computed is not None:
+                if comp is None:
+                    raise ValueError("computed expert outputs need compute_mask")
+                if computed.shape != (bs, top_k, values.shape[-1]) or computed.dtype != values.dtype or \
+                        computed.stride(-1) != 1:
+                    raise ValueError("computed: [bs, top_k, H] in the value dtype with unit inner stride")
+                rc = self._lib.alut_lookup_combine_experts(
+                    tables, batch, params, w.data_ptr(), w.stride(0), comp.data_ptr(), comp.stride(0),
+                    computed.data_ptr(), computed.stride(0), computed.stride(1), rn, int(accumulate), out.data_ptr(),
+                    out.stride(0), _alut.dtype_code(out.dtype), _alut.ptr(hit), _alut.ptr(idx), hs, ws.data_ptr(),
+                    ws.numel(), _alut.stream_ptr(self.device))
+                _alut.check(rc, "alut_lookup_combine_experts")
+            else:
+                rc = self._lib.alut_lookup_combine(
+                    tables, batch, params, w.data_ptr(), w.stride(0), _alut.ptr(comp),
+                    0 if comp is None else comp.stride(0), rn, int(accumulate), out.data_ptr(), out.stride(0),
+                    _alut.dtype_code(out.dtype), _alut.ptr(hit), _alut.ptr(idx), hs, ws.data_ptr(), ws.numel(),
+                    _alut.stream_ptr(self.device))
+                _alut.check(rc, "alut_lookup_combine")
             if CacheConfig.ALUT_CHECK_ERRORS:
                 self.check_device_errors("alut_lookup_combine")
         elif not accumulate:

@@ -30,7 +30,7 @@ ULP = rules.ULP
 
 def golden_names():
     """Search/combine fixtures (the online-window fixtures are online_*.npz)."""
-    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(("online_", "route_")))
+    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(("online_", "route_", "manager_")))
 
 
 def online_names():
