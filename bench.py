@@ -583,8 +583,9 @@ def c4_workload(args, device, flush, peaks, checker):
 def c5_workload(args, rank, world, device, flush, peaks, checker):
     """The large single table (K=65536, L=128 fp32 keys, 65536 x 4096 bf16 rows) sharded by
     centroid range over the ranks; 32768 tokens (hidden 4096, bf16) looked up per step:
-    local tensor-core scan, NCCL all-gather of packed candidates, merge, owner gather.
-    Strong scaling: the same tokens and table at every N."""
+    projection of this rank's tokens, NCCL all-gather of the queries, local tensor-core scan,
+    all-gather of packed candidates, merge, peer row gather; the step is one CUDA graph
+    (NCCL calls included). Strong scaling: the same tokens and table at every N."""
     from table_moe.cache_engine.sharded import ShardedCentroidTable, shard_range
 
     c = C5
@@ -599,16 +600,14 @@ def c5_workload(args, rank, world, device, flush, peaks, checker):
     gv = torch.Generator(device=device).manual_seed(6006 + rank)
     values = torch.randn(1, 2, k1 - k0, c["h"], generator=gv, device=device, dtype=torch.bfloat16).mul_(0.05)
     table = ShardedCentroidTable(keys, values, pca, c["k"])
-
-    def step():
-        table.lookup(x, vis)
+    graph, (hit, idx, rows) = table.capture(x, vis)  # the whole lookup, NCCL calls included
 
     barrier(world)
-    total_ms, _ = timed_steps(step, args.wl_steps, args.warmup, device, flush)
+    total_ms, _ = timed_steps(graph.replay, args.wl_steps, args.warmup, device, flush)
     total_ms = max_over_ranks(total_ms, world, device)
     # Checker: the winners of a token sample against the oracle over the full table, and the
     # rows of this rank's sampled tokens against the owning shard's (regenerated) values.
-    hit, idx, rows = table.lookup(x, vis)
+    graph.replay()
     torch.cuda.synchronize()
     n = c["tokens"] // world
     lo = rank * n
@@ -635,6 +634,7 @@ def c5_workload(args, rank, world, device, flush, peaks, checker):
             ref[own] = vr[0, 1, gi[own] - r0]
             del vr
     checker.rows("c5", bits16(rows[(mine - lo).to(device)]), bits16(ref))
+    del graph
     table.close()
     flops = c["tokens"] * c["k"] * c["l"] * 2
     t = total_ms / args.wl_steps / 1e3

@@ -18,6 +18,13 @@ rows. A lookup of Q tokens then runs in three steps:
    (zeros elsewhere) and a reduce-scatter (sum) hands out the token slices - a row has
    one non-zero contribution, so the sum is an exact copy.
 
+Failure detection (``timeout_s``): every collective of a lookup is waited on with that
+limit and a timed-out wait raises ``ShardTimeoutError`` (a ``TimeoutError``); a rank that
+leaves calls ``leave()`` between lookups, which the other ranks see in the process group's
+store before their next launch (``PeerLeftError``). Either error marks the table failed.
+``capture()`` records one whole lookup (NCCL calls included) as a CUDA graph, so that the
+per-call host work - argument marshalling, launches, collective calls - is paid once.
+
 The reference is single-GPU; this is the centroid-range sharding the benchmark's large-
 table configuration asks for. The device work goes through the C ABI; the three device
 steps are attributes of the object so that the exchange logic can be exercised on CPU
@@ -26,11 +33,23 @@ process groups (gloo) with stand-ins.
 from __future__ import annotations
 
 import ctypes
+import time
+from datetime import timedelta
 
 import torch
 import torch.distributed as dist
 
 from . import _alut
+
+_LEFT_KEY = "alut_sharded_table/left"
+
+
+class PeerLeftError(RuntimeError):
+    """A rank of the table's group left (``leave()``) before this lookup."""
+
+
+class ShardTimeoutError(TimeoutError):
+    """A collective of the sharded lookup did not complete within ``timeout_s``."""
 
 
 def shard_range(k_total: int, world: int, rank: int):
@@ -40,10 +59,21 @@ def shard_range(k_total: int, world: int, rank: int):
 
 class ShardedCentroidTable:
     def __init__(self, keys, values, pca, k_total, *, group=None, keyset=_alut.KEYS_RAW,
-                 normalize=False, cmp_ge=False, thr_vision=0.0, thr_text=0.0, eps=1e-6):
+                 normalize=False, cmp_ge=False, thr_vision=0.0, thr_text=0.0, eps=1e-6, timeout_s=None,
+                 store=None):
         """keys: [1, 2, Kr, L] this rank's slice (rows shard_range(k_total, W, r));
-        values: [1, 2, Kr, H]; pca: {"vision": {proj, bias}, "text": {...}}."""
+        values: [1, 2, Kr, H]; pca: {"vision": {proj, bias}, "text": {...}}.
+        timeout_s: limit of every collective wait (None: the process group's own timeout);
+        store: the store ``leave()`` announces through (default: the default group's)."""
         self.group = group
+        self.timeout = None if timeout_s is None else timedelta(seconds=float(timeout_s))
+        self._store = store
+        if self._store is None and dist.is_initialized() and timeout_s is not None:
+            self._store = dist.distributed_c10d._get_default_store()
+        self._left_seen = 0
+        self.failed = None
+        self._bufs = {}
+        self._capturing = False
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.k_total = int(k_total)
@@ -93,20 +123,36 @@ class ShardedCentroidTable:
         p = self.params
         return _alut.make_params(p["keyset"], p["normalize"], p["cmp_ge"], p["thr_vision"], p["thr_text"], p["eps"])
 
+    def _buf(self, q, name, shape, dtype, zero=False):
+        """Per-batch-size buffers, made once (also what a captured lookup replays on)."""
+        key = (q, name)
+        t = self._bufs.get(key)
+        if t is None or t.shape != torch.Size(shape) or t.dtype != dtype:
+            t = (torch.zeros if zero else torch.empty)(shape, dtype=dtype, device=self.device)
+            self._bufs[key] = t
+        return t
+
+    def _workspace(self, q):
+        lib = _alut.load()
+        need = int(lib.alut_workspace_size(self._tables_struct(), q, 1))
+        if self._ws is None or self._ws.numel() < need:
+            if self._capturing:
+                raise RuntimeError("sharded lookup: workspace must be sized before capture (run lookup once)")
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
     def _local_search(self, x, is_vision):
         """Packed best candidate of every token over this rank's slice -> int64 [Q]."""
         lib = _alut.load()
         q = x.shape[0]
         t = self._tables_struct()
-        need = int(lib.alut_workspace_size(t, q, 1))
-        if self._ws is None or self._ws.numel() < need:
-            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
-        sel = torch.zeros(q, 1, dtype=torch.int64, device=self.device)
-        vis = is_vision.reshape(-1).bool().contiguous()
-        packed = torch.empty(q, dtype=torch.int64, device=self.device)
+        ws = self._workspace(q)
+        sel = self._buf(q, "sel", (q, 1), torch.int64, zero=True)
+        vis = is_vision.reshape(-1)
+        packed = self._buf(q, "packed", (q,), torch.int64)
         b = _alut.make_batch(x, sel, vis, None)  # x, sel, vis stay referenced until the call returns
         rc = lib.alut_search_packed(t, ctypes.byref(b), self._params_struct(), None, self.k0, packed.data_ptr(),
-                                    self._ws.data_ptr(), self._ws.numel(), _alut.stream_ptr(self.device))
+                                    ws.data_ptr(), ws.numel(), _alut.stream_ptr(self.device))
         _alut.check(rc, "alut_search_packed")
         return packed
 
@@ -114,9 +160,9 @@ class ShardedCentroidTable:
         """[W, Q] packed candidates -> (hit [Q] bool, idx [Q] int64 global)."""
         lib = _alut.load()
         w, q = packed_all.shape
-        vis = is_vision.reshape(-1).bool().contiguous()
-        hit = torch.empty(q, dtype=torch.bool, device=self.device)
-        idx = torch.empty(q, dtype=torch.int64, device=self.device)
+        vis = is_vision.reshape(-1)
+        hit = self._buf(q, "hit", (q,), torch.bool)
+        idx = self._buf(q, "idx", (q,), torch.int64)
         rc = lib.alut_merge_packed(w, q, 1, packed_all.data_ptr(), vis.data_ptr(), self._params_struct(),
                                    hit.data_ptr(), idx.data_ptr(), _alut.stream_ptr(self.device))
         _alut.check(rc, "alut_merge_packed")
@@ -139,25 +185,58 @@ class ShardedCentroidTable:
     def _nccl(self):
         return self.world > 1 and self.device.type == "cuda" and dist.get_backend(self.group) == "nccl"
 
+    # ---- collectives with failure detection ---------------------------------------------
+    def _precheck(self):
+        """Before a lookup's first launch: fail fast if a peer left (store) or a previous
+        lookup failed."""
+        if self.failed:
+            raise PeerLeftError(f"sharded table is unusable: {self.failed}")
+        if self._store is not None and self.world > 1 and not self._capturing:
+            left = int(self._store.add(_LEFT_KEY, 0))
+            if left > self._left_seen:
+                self.failed = f"{left} rank(s) left the group"
+                raise PeerLeftError(self.failed)
+
+    def _all_gather(self, out, inp):
+        if self._capturing or self.timeout is None:
+            dist.all_gather_into_tensor(out, inp, group=self.group)
+            return
+        t0 = time.monotonic()
+        work = dist.all_gather_into_tensor(out, inp, group=self.group, async_op=True)
+        try:
+            work.wait(timeout=self.timeout)
+        except RuntimeError as exc:
+            waited = time.monotonic() - t0
+            if waited >= 0.9 * self.timeout.total_seconds():
+                self.failed = f"collective timed out after {waited:.2f} s: {exc}"
+                raise ShardTimeoutError(self.failed) from exc
+            self.failed = f"collective failed after {waited:.2f} s (a peer is gone): {exc}"
+            raise PeerLeftError(self.failed) from exc
+
+    def leave(self):
+        """Announce, between lookups, that this rank stops taking part (the other ranks'
+        next lookup raises PeerLeftError instead of waiting for it)."""
+        if self._store is not None:
+            self._store.add(_LEFT_KEY, 1)
+        self.failed = "this rank left the group"
+
     def _project_split(self, x, is_vision):
         """This rank projects its Q/W tokens; the ranks all-gather the queries -> [Q, L] fp32."""
         lib = _alut.load()
         q = x.shape[0]
         lo, hi = q * self.rank // self.world, q * (self.rank + 1) // self.world
         t = self._tables_struct()
-        need = int(lib.alut_workspace_size(t, q, 1))
-        if self._ws is None or self._ws.numel() < need:
-            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        ws = self._workspace(q)
         xs = x[lo:hi]
-        vs = is_vision.reshape(-1)[lo:hi].bool().contiguous()
-        sel = torch.zeros(hi - lo, 1, dtype=torch.int64, device=self.device)
-        mine = torch.empty(hi - lo, t.l, dtype=torch.float32, device=self.device)
+        vs = is_vision.reshape(-1)[lo:hi]
+        sel = self._buf(q, "sel_mine", (hi - lo, 1), torch.int64, zero=True)
+        mine = self._buf(q, "q_mine", (hi - lo, t.l), torch.float32)
         b = _alut.make_batch(xs, sel, vs, None)  # xs, sel, vs stay referenced until the call returns
         _alut.check(lib.alut_project(t, ctypes.byref(b), int(self.params["normalize"]), self.params["eps"],
-                                     mine.data_ptr(), t.l, self._ws.data_ptr(), self._ws.numel(),
+                                     mine.data_ptr(), t.l, ws.data_ptr(), ws.numel(),
                                      _alut.stream_ptr(self.device)), "alut_project")
-        q_all = torch.empty(q, t.l, dtype=torch.float32, device=self.device)
-        dist.all_gather_into_tensor(q_all, mine, group=self.group)
+        q_all = self._buf(q, "q_all", (q, t.l), torch.float32)
+        self._all_gather(q_all, mine)
         return q_all
 
     def _local_search_q(self, q_all, is_vision):
@@ -166,17 +245,15 @@ class ShardedCentroidTable:
         lib = _alut.load()
         q = q_all.shape[0]
         t = self._tables_struct()
-        need = int(lib.alut_workspace_size(t, q, 1))
-        if self._ws is None or self._ws.numel() < need:
-            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
-        sel = torch.zeros(q, 1, dtype=torch.int64, device=self.device)
-        vis = is_vision.reshape(-1).bool().contiguous()
-        packed = torch.empty(q, dtype=torch.int64, device=self.device)
+        ws = self._workspace(q)
+        sel = self._buf(q, "sel", (q, 1), torch.int64, zero=True)
+        vis = is_vision.reshape(-1)
+        packed = self._buf(q, "packed", (q,), torch.int64)
         b = _alut.make_batch(None, sel, vis, None)
         p = self.params
         prm = _alut.make_params(p["keyset"], False, p["cmp_ge"], p["thr_vision"], p["thr_text"], p["eps"])
         rc = lib.alut_search_packed(t, ctypes.byref(b), prm, q_all.data_ptr(), self.k0, packed.data_ptr(),
-                                    self._ws.data_ptr(), self._ws.numel(), _alut.stream_ptr(self.device))
+                                    ws.data_ptr(), ws.numel(), _alut.stream_ptr(self.device))
         _alut.check(rc, "alut_search_packed")
         return packed
 
@@ -236,36 +313,48 @@ class ShardedCentroidTable:
     def _gather_peer(self, hit, idx, is_vision, lo, hi):
         lib = _alut.load()
         ptrs, starts, strides_m, _opened, stride_k = self._peers
+        q = hit.shape[0]
         n = hi - lo
         h = self.values.shape[-1]
-        out = torch.empty(n, h, dtype=self.values.dtype, device=self.device)
-        vis = is_vision.reshape(-1)[lo:hi].bool().contiguous()
-        rc = lib.alut_gather_rows_sharded(n, hit[lo:hi].contiguous().data_ptr(), idx[lo:hi].contiguous().data_ptr(),
-                                          vis.data_ptr(), self.world, ptrs.data_ptr(), starts.data_ptr(),
-                                          strides_m.data_ptr(), stride_k, h, _alut.dtype_code(self.values.dtype),
-                                          out.data_ptr(), out.stride(0), _alut.stream_ptr(self.device))
+        out = self._buf(q, "rows", (n, h), self.values.dtype)
+        vis = is_vision.reshape(-1)[lo:hi]
+        rc = lib.alut_gather_rows_sharded(n, hit[lo:hi].data_ptr(), idx[lo:hi].data_ptr(), vis.data_ptr(), self.world,
+                                          ptrs.data_ptr(), starts.data_ptr(), strides_m.data_ptr(), stride_k, h,
+                                          _alut.dtype_code(self.values.dtype), out.data_ptr(), out.stride(0),
+                                          _alut.stream_ptr(self.device))
         _alut.check(rc, "alut_gather_rows_sharded")
         return out
 
     # ---- lookup ---------------------------------------------------------------------------
     def search(self, x, is_vision):
         """Global (hit, idx) of every token, identical on all ranks."""
+        self._precheck()
+        is_vision = is_vision.reshape(-1)
+        if is_vision.dtype != torch.bool or not is_vision.is_contiguous():
+            is_vision = is_vision.bool().contiguous()
         if self._nccl() and x.shape[0] % self.world == 0 and self.local_search == self._local_search:
             packed = self._local_search_q(self._project_split(x, is_vision), is_vision)
         else:
             packed = self.local_search(x, is_vision)
         if self.world == 1:
             return self.merge(packed.view(1, -1), is_vision)
-        flat = torch.empty(self.world * packed.numel(), dtype=packed.dtype, device=packed.device)
-        dist.all_gather_into_tensor(flat, packed.contiguous(), group=self.group)
+        q = packed.numel()
+        flat = self._buf(q, "flat", (self.world * q,), packed.dtype) if packed.device == self.device else \
+            torch.empty(self.world * q, dtype=packed.dtype, device=packed.device)
+        self._all_gather(flat, packed.contiguous())
         return self.merge(flat.view(self.world, -1), is_vision)
 
     def lookup(self, x, is_vision):
         """Search, then the value rows of this rank's token slice [Q*r/W, Q*(r+1)/W) (Q must
-        be a multiple of W): (hit [Q], idx [Q], rows [Q/W, H])."""
+        be a multiple of W): (hit [Q], idx [Q], rows [Q/W, H]). The returned tensors are
+        this table's buffers for batches of Q tokens: the next lookup of the same size
+        overwrites them."""
         q = x.shape[0]
         if self.world > 1 and q % self.world:
             raise ValueError(f"token count {q} is not a multiple of the world size {self.world}")
+        is_vision = is_vision.reshape(-1)
+        if is_vision.dtype != torch.bool or not is_vision.is_contiguous():
+            is_vision = is_vision.bool().contiguous()
         hit, idx = self.search(x, is_vision)
         direct = self.world == 1 and self.device.type == "cuda"
         if (direct or self._nccl()) and self.gather_owned == self._gather_owned and self._peer_setup():
@@ -282,3 +371,27 @@ class ShardedCentroidTable:
         mine = torch.empty(n, rows.shape[1], dtype=rows.dtype, device=rows.device)
         dist.reduce_scatter_tensor(mine, rows.contiguous(), op=dist.ReduceOp.SUM, group=self.group)
         return hit, idx, mine
+
+    def capture(self, x, is_vision):
+        """Record one lookup of this (static) x / is_vision as a CUDA graph: returns
+        (graph, (hit, idx, rows)); ``graph.replay()`` reruns it into the same tensors. Every
+        rank of the group captures together (the NCCL calls are part of the graph)."""
+        if self.device.type != "cuda":
+            raise ValueError("capture needs a CUDA table")
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):  # sizes buffers and the workspace, maps the peers
+            for _ in range(2):
+                self.lookup(x, is_vision)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        graph = torch.cuda.CUDAGraph()
+        self._capturing = True
+        try:
+            with torch.cuda.graph(graph):
+                outs = self.lookup(x, is_vision)
+        finally:
+            self._capturing = False
+        return graph, outs

@@ -98,3 +98,21 @@ def test_sharded_world2_nccl_matches_search():
     for r in range(world):
         hit, idx, rows = out[r]
         _check(hit, idx, rows, ref_hit, ref_idx, values, vis, Q * r // world, Q * (r + 1) // world)
+
+
+def test_sharded_world1_captured_graph_matches_eager():
+    """The whole sharded lookup captured as a CUDA graph gives the eager results."""
+    from table_moe.cache_engine.sharded import ShardedCentroidTable
+
+    dev = torch.device("cuda:0")
+    keys, values, proj, x, vis = _tables(dev)
+    pca = {m: {"proj": proj[i].to(dev), "bias": torch.zeros(L, device=dev)} for i, m in enumerate(("vision", "text"))}
+    t = ShardedCentroidTable(keys.to(dev), values.to(dev), pca, K)
+    xd, vd = x.to(dev), vis.to(dev)
+    h0, i0, r0 = (a.clone() for a in t.lookup(xd, vd))
+    graph, (h1, i1, r1) = t.capture(xd, vd)
+    h1.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(h0, h1) and torch.equal(i0, i1) and torch.equal(r0.view(torch.int16), r1.view(torch.int16))
+    t.close()

@@ -112,3 +112,67 @@ def test_shard_ranges_cover_the_table():
             spans = [shard_range(K, W, r) for r in range(W)]
             assert spans[0][0] == 0 and spans[-1][1] == K
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+
+
+def _failing_worker(rank, world, port, scenario, out):
+    """Rank 1 stops after one lookup; rank 0's next lookup must end with an error within the
+    limit instead of waiting: 'leave' announces it through the store, 'silent' just stops
+    (rank 0's collective times out)."""
+    import time
+
+    from table_moe.cache_engine.sharded import PeerLeftError, ShardTimeoutError
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    store = dist.distributed_c10d._get_default_store()
+    q, keys, values, vis = _problem()
+    K = keys.shape[0]
+    k0, k1 = shard_range(K, world, rank)
+    shard_keys = torch.from_numpy(keys[k0:k1]).view(1, 1, k1 - k0, -1).expand(1, 2, -1, -1).contiguous()
+    shard_vals = torch.from_numpy(values[k0:k1]).view(1, 1, k1 - k0, -1).expand(1, 2, -1, -1).contiguous()
+    t = ShardedCentroidTable(shard_keys, shard_vals, pca={}, k_total=K, timeout_s=2.0)
+    t.local_search = lambda x, v: torch.from_numpy(_pack(np.zeros(len(x), np.float32), np.full(len(x), t.k0)))
+    t.merge = lambda p, v: (torch.ones(p.shape[1], dtype=torch.bool), p[0] & 0)
+    t.gather_owned = lambda h, i, v: torch.zeros(len(h), shard_vals.shape[-1])
+    t.lookup(torch.from_numpy(q), torch.from_numpy(vis))  # one good step on both ranks
+    if rank == 1:
+        if scenario == "leave":
+            t.leave()
+        store.set("rank1_stopped", "1")
+        store.wait(["rank0_done"], __import__("datetime").timedelta(seconds=30))
+        out[rank] = "stopped"
+        return
+    store.wait(["rank1_stopped"])
+    t0 = time.monotonic()
+    try:
+        t.lookup(torch.from_numpy(q), torch.from_numpy(vis))
+        out[rank] = ("no error", time.monotonic() - t0)
+    except PeerLeftError as exc:
+        out[rank] = ("left", time.monotonic() - t0, str(exc))
+    except ShardTimeoutError as exc:
+        out[rank] = ("timeout", time.monotonic() - t0, str(exc))
+    try:  # the table stays failed: no further collective is attempted
+        t.lookup(torch.from_numpy(q), torch.from_numpy(vis))
+        out["again"] = "no error"
+    except PeerLeftError:
+        out["again"] = "refused"
+    store.set("rank0_done", "1")
+
+
+@pytest.mark.timeout(120)
+@pytest.mark.parametrize("scenario,expect,limit", [("leave", "left", 1.0), ("silent", "timeout", 10.0)])
+def test_sharded_lookup_fails_fast_when_a_rank_stops(scenario, expect, limit):
+    world = 2
+    out = mp.get_context("spawn").Manager().dict()
+    ctx = mp.start_processes(_failing_worker, args=(world, _free_port(), scenario, out), nprocs=world,
+                             start_method="spawn", join=False)
+    while not ctx.join(timeout=60):
+        pass
+    assert out[1] == "stopped"
+    kind, elapsed = out[0][0], out[0][1]
+    assert kind == expect, out[0]
+    assert elapsed < limit
+    if scenario == "silent":
+        assert elapsed >= 1.5  # it waited for the limit, not for ever
+    assert out["again"] == "refused"
