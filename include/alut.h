@@ -31,9 +31,19 @@
  *                         table_moe/skip/pruning.py:55 renormalize_surviving_weights
  *   alut_lookup_combine   search + combine in one call (no single reference counterpart;
  *                         it chains search.py:808 and cached_layers.py:340-465)
+ *   alut_lookup_combine_experts
+ *                         cached_layers.py:340-465 whole (lookups + computed experts' outputs)
+ *   alut_route            table_moe/ops/qwen_topk_softmax.py:122-153 + cached_layers.py:69-84
+ *   alut_keep_mask        table_moe/skip/pruning.py:18-48 build_prefill_keep_mask
+ *   alut_normalize_rows   table_moe/cache_engine/manager.py:24-31, :205-207
  *   alut_search_packed /
  *   alut_merge_packed     centroid-range sharding of one large table (new: the reference
  *                         is single-GPU; the merge rule is the tie rule of search.py:89)
+ *
+ * Input ordering: batches of <= 32 tokens (the decode chain) read sel, reuse and is_vision
+ * before waiting for the kernel that precedes the call on the stream, so that key copies
+ * start early; these inputs must be complete when the call is issued (true for inputs
+ * written by ordinary stream-ordered work). x is read only after that wait.
  */
 #ifndef ALUT_H_
 #define ALUT_H_
