@@ -412,9 +412,13 @@ static int launch_combine_t(bool vec, const CombineArgs& a, dim3 grid, cudaStrea
 
 template <typename TK>
 static int launch_search_decode_t(const DecodeScanArgs& d, dim3 grid, size_t smem, cudaStream_t st) {
-  int rc = allow_smem(reinterpret_cast<const void*>(k_search_decode<TK>), smem);
+  // Ranks with a compile-time specialisation (the row lives in registers); others generic.
+  auto kern = d.s.l == 64 ? k_search_decode<TK, 64>
+                          : (d.s.l == 96 ? k_search_decode<TK, 96> : (d.s.l == 128 ? k_search_decode<TK, 128>
+                                                                                   : k_search_decode<TK, 0>));
+  int rc = allow_smem(reinterpret_cast<const void*>(kern), smem);
   if (rc) return rc;
-  cudaError_t e = launch_pdl(k_search_decode<TK>, grid, dim3(kSearchThreads), smem, st, d);
+  cudaError_t e = launch_pdl(kern, grid, dim3(kSearchThreads), smem, st, d);
   if (e != cudaSuccess) return fail(ALUT_ECUDA, "k_search_decode: %s", cudaGetErrorString(e));
   return check_launch("k_search_decode");
 }
@@ -542,6 +546,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
   const Workspace wt = workspace_layout(b->q, b->s, t->l, 2 * t->num_experts, true);
   if (ksplit && tc_tables_ok(t) && vec && tc_scan_wanted(pairs, 2 * t->num_experts) && ws_bytes >= wt.total) {
     a.group = kTcRows;
+    a.cand_cnt = reinterpret_cast<int*>(base + wt.cand_cnt);
     int rc = launch_plan(a, reinterpret_cast<int*>(base + w.tabs), st);
     if (rc) return rc;
     if (!q_direct) rc = launch_project(t->key_dtype, b->x_dtype, a, st);
@@ -570,6 +575,8 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     c.meta = a.meta;
     c.best = best;
     c.err = a.meta + 1;
+    c.cand_cnt = a.cand_cnt;
+    c.cand = reinterpret_cast<int*>(base + wt.cand);
     {
       const int64_t units = wt.tc_groups * kTcRows * (t->l / 8);
       const int grid = static_cast<int>(std::min<int64_t>((units + 255) / 256, static_cast<int64_t>(num_sms()) * 8));
@@ -586,6 +593,28 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     k_search_tc<<<num_sms(), kTcThreads, smem, st>>>(c);
     rc = check_launch("k_search_tc");
     if (rc) return rc;
+    {
+      TcRescoreArgs r{};
+      r.keys = c.keys;
+      r.key_stride_e = c.key_stride_e;
+      r.key_stride_m = c.key_stride_m;
+      r.key_stride_k = c.key_stride_k;
+      r.l = t->l;
+      r.s = b->s;
+      r.num_experts = t->num_experts;
+      r.pairs = pairs;
+      r.idx_offset = idx_offset;
+      r.qlow = a.qlow;
+      r.sel = b->sel;
+      r.sel_stride = b->sel_stride;
+      r.is_vision = b->is_vision;
+      r.cand_cnt = c.cand_cnt;
+      r.cand = c.cand;
+      r.best = best;
+      k_tc_rescore<<<static_cast<unsigned>((static_cast<int64_t>(pairs) * 16 + 255) / 256), 256, 0, st>>>(r);
+      rc = check_launch("k_tc_rescore");
+      if (rc) return rc;
+    }
     if (g_prof_start && g_prof_stop && record_profile(g_prof_stop, st)) return ALUT_ECUDA;
     return ALUT_OK;
   }

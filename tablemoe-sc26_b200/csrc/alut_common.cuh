@@ -22,6 +22,8 @@ constexpr int kSearchGroup = 32;         // (token, slot) pairs scored per searc
 // Slots per search group of the CUDA-core scans of large batches: kSearchGroup, or
 // kCcSmallGroup when the batch would otherwise give fewer (group, chunk) tiles than SMs.
 constexpr int kCcSmallGroup = 8;
+// Candidate rows per slot the tensor-core scan hands to its exact rescoring pass.
+constexpr int kTcCandGlobal = 16;
 constexpr int kMaxTables = 4096;         // 2 * num_experts
 constexpr int kMaxSlots = 64;            // top_k
 constexpr int kCombineThreads = 64;      // 8 elements per thread -> 512 per CTA
@@ -222,6 +224,8 @@ struct Workspace {
   // staged per group of <= 128 slots as bf16 operand tiles, and their norms.
   size_t qsplit;    // bf16   [tc_groups][128 * L]
   size_t qnorm;     // f32    [tc_groups][128]
+  size_t cand_cnt;  // int32  [Q * S]        candidates of each slot left for the rescoring pass
+  size_t cand;      // int32  [Q * S][kTcCandGlobal] their centroid rows
   size_t total;
   int64_t max_groups;
   int64_t tc_groups;
@@ -263,6 +267,8 @@ inline Workspace workspace_layout(int q, int s, int l, int num_tables, bool tc =
     w.tc_groups = (pairs + 127) / 128 + (pairs < num_tables ? pairs : num_tables) + 1;
     w.qsplit = off; off = align256(off + static_cast<size_t>(w.tc_groups) * 128 * l * 2);
     w.qnorm = off;  off = align256(off + sizeof(float) * w.tc_groups * 128);
+    w.cand_cnt = off; off = align256(off + sizeof(int32_t) * (pairs + 1));
+    w.cand = off;   off = align256(off + sizeof(int32_t) * kTcCandGlobal * (pairs + 1));
   }
   w.total = off;
   return w;

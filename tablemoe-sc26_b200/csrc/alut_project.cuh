@@ -47,6 +47,8 @@ struct ProjPlanArgs {
   int* sorted;
   int4* groups;
   int* meta;
+  // tensor-core scan: per-slot candidate counters, cleared with `best` (NULL otherwise)
+  int* cand_cnt;
   // tensor-core projection: bf16 split basis [2][3][L][H] (see alut_prepare_basis)
   const __nv_bfloat16* proj_split;
   // plan: slots per search group (kSearchGroup for the CUDA-core scans, 128 for the
@@ -137,6 +139,7 @@ __global__ void __launch_bounds__(kProjThreads) k_plan(ProjPlanArgs a) {
   for (int p = tid; p < pairs; p += kProjThreads) {
     tab_of[p] = plan_table(a, p, &bad);
     a.best[p] = 0ull;
+    if (a.cand_cnt) a.cand_cnt[p] = 0;
   }
   if (bad) atomicOr(&a.meta[1], kErrBadExpert);
   __syncthreads();
@@ -198,6 +201,7 @@ __global__ void __launch_bounds__(256) k_plan_count(ProjPlanArgs a, int* counts)
     int t = -1;
     if (p < pairs) {
       a.best[p] = 0ull;
+      if (a.cand_cnt) a.cand_cnt[p] = 0;
       t = plan_table(a, p, &bad);
     }
     const unsigned same = __match_any_sync(0xffffffffu, t);

@@ -380,9 +380,9 @@ struct DecodeScanArgs {
   const uint8_t* reuse;
   int64_t reuse_stride;
   int* err;
-  // Optional (lookup + combine): value rows of the tables, in bytes. A CTA whose chunk
-  // candidate becomes a slot's best so far asks L2 to fetch that centroid's value row, so
-  // the combine that follows reads the winners from L2 instead of HBM.
+  // Optional (lookup + combine): value rows of the tables, in bytes. Every CTA asks L2 to
+  // fetch the value row of its chunk's best candidate of each slot, so the combine that
+  // follows reads the winners from L2 instead of HBM.
   const unsigned char* values;
   int64_t vs_e, vs_m, vs_k;
   uint32_t row_bytes;
@@ -392,8 +392,11 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) 
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-template <typename TK>
-__global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs d) {
+// LC: L fixed at compile time (64, 96, 128: the row is scored from registers), 0 for any
+// other L. Each rank is its own kernel so that registers are sized for that rank alone;
+// 4 CTAs per SM stay resident (3 at L = 128, whose row alone takes 128 registers).
+template <typename TK, int LC>
+__global__ void __launch_bounds__(kSearchThreads, LC == 128 ? 3 : 4) k_search_decode(DecodeScanArgs d) {
   extern __shared__ __align__(128) unsigned char sm[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
   const SearchArgs& a = d.s;
@@ -480,10 +483,8 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
   ALUT_TRACE(13);
   const bool ok = mbar_try_wait(&bar[0], 0);
   const TK* row = reinterpret_cast<const TK*>(kbuf + static_cast<size_t>(tid) * pitch);
-  if (L == 64)
-    score_row_fixed<TK, 64>(row, ok && tid < rows, qs, cnt, chunk * kSearchChunkK, red_s, red_k);
-  else if (L == 128)
-    score_row_fixed<TK, 128>(row, ok && tid < rows, qs, cnt, chunk * kSearchChunkK, red_s, red_k);
+  if constexpr (LC > 0)
+    score_row_fixed<TK, LC>(row, ok && tid < rows, qs, cnt, chunk * kSearchChunkK, red_s, red_k);
   else
     score_row<TK, true>(row, ok && tid < rows, qs, L, cnt, chunk * kSearchChunkK, red_s, red_k);
   __syncthreads();
@@ -499,9 +500,8 @@ __global__ void __launch_bounds__(kSearchThreads) k_search_decode(DecodeScanArgs
       }
     }
     if (b) {
-      const uint64_t old = atomicMax(reinterpret_cast<unsigned long long*>(a.best + pid[tid]),
-                                     static_cast<unsigned long long>(b));
-      if (d.values && b > old)
+      atomicMax(reinterpret_cast<unsigned long long*>(a.best + pid[tid]), static_cast<unsigned long long>(b));
+      if (d.values)  // every chunk's winner: waiting for the atomic's old value would delay the exit
         prefetch_l2_bulk(d.values + static_cast<int64_t>(table >> 1) * d.vs_e + static_cast<int64_t>(table & 1) * d.vs_m +
                              static_cast<int64_t>(cand_index(b) - a.idx_offset) * d.vs_k,
                          d.row_bytes);

@@ -280,7 +280,9 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
 
 // Exact fp32 score of one centroid row: sequential fmaf over l (the CUDA-core scans' order).
 // L % 16 == 0: rows are read 32 values (8 float4 of each) at a time, all in flight before
-// the dependent FMAs.
+// the dependent FMAs. Used by the in-kernel rescoring and by k_tc_rescore alike, so every
+// candidate of a slot is scored by one arithmetic (exact duplicate rows tie to the lowest
+// index).
 __device__ __forceinline__ float tc_exact(const float* q, const float* kp, int L) {
   float e = 0.f;
   for (int l0 = 0; l0 < L; l0 += 32) {
@@ -368,6 +370,8 @@ struct TcArgs {
   const int* meta;
   uint64_t* best;
   int* err;
+  int* cand_cnt;  // [pairs] candidates handed to k_tc_rescore (cleared by the plan)
+  int* cand;      // [pairs][kTcCandGlobal] their rows (within this table)
 };
 
 #ifdef ALUT_PHASE_TRACE
@@ -664,14 +668,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
         }
         TC_ACC(43);
         if (tile + 1 == t_end || c == a.nchunks - 1) {
+          // End of this CTA's part of the group: the surviving candidates go to the rescoring
+          // pass (k_tc_rescore) instead of being rescored here, where each one would hold
+          // the accumulators for a dependent global load; a full list rescored here.
           TC_T0();
           unsigned long long mine = s_mine[e];
           for (int i = 0; i < n; ++i) {
             if (s_cv[i * kTcEpiThreads + e] < amax - tw) continue;
-            const unsigned long long cand =
-                tc_rescore(q, kt, a.key_stride_k, L, s_cc[i * kTcEpiThreads + e], a.idx_offset);
-            TC_COUNT();
-            mine = cand > mine ? cand : mine;
+            const int pos = atomicAdd(a.cand_cnt + p, 1);
+            if (pos < kTcCandGlobal) {
+              a.cand[static_cast<int64_t>(p) * kTcCandGlobal + pos] = s_cc[i * kTcEpiThreads + e];
+            } else {
+              const unsigned long long cand =
+                  tc_rescore(q, kt, a.key_stride_k, L, s_cc[i * kTcEpiThreads + e], a.idx_offset);
+              TC_COUNT();
+              mine = cand > mine ? cand : mine;
+            }
           }
           n = 0;
           if (mine) atomicMax(reinterpret_cast<unsigned long long*>(a.best + p), mine);
@@ -703,6 +715,53 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
   __syncthreads();
   if (warp == kTcMmaWarp)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
+}
+
+// The exact fp32 rescoring of the tensor-core scan's candidates: one thread per (slot,
+// candidate) - 16 lanes per slot - each computing tc_exact, then the slot's maximum over its
+// half-warp and one packed atomicMax, as the scan folds its own.
+struct TcRescoreArgs {
+  const float* keys;
+  int64_t key_stride_e, key_stride_m, key_stride_k;
+  int l, s, num_experts;
+  int64_t pairs;
+  uint32_t idx_offset;
+  const float* qlow;
+  const int64_t* sel;
+  int64_t sel_stride;
+  const uint8_t* is_vision;
+  const int* cand_cnt;
+  const int* cand;
+  uint64_t* best;
+};
+
+static_assert(kTcCandGlobal == 16, "k_tc_rescore gives each slot a half-warp");
+
+__global__ void __launch_bounds__(256) k_tc_rescore(TcRescoreArgs a) {
+  const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t p = gt >> 4;  // slot
+  const int i = static_cast<int>(gt & 15);
+  unsigned long long c = 0ull;
+  if (p < a.pairs) {
+    const int n = min(a.cand_cnt[p], kTcCandGlobal);
+    if (i < n) {
+      const int64_t t = p / a.s;
+      const int64_t e = a.sel[t * a.sel_stride + p % a.s];
+      if (e >= 0 && e < a.num_experts) {
+        const int table = static_cast<int>(e) * 2 + (a.is_vision[t] ? 0 : 1);
+        const int kr = a.cand[p * kTcCandGlobal + i];
+        const float* kp = a.keys + static_cast<int64_t>(table >> 1) * a.key_stride_e +
+                          static_cast<int64_t>(table & 1) * a.key_stride_m + static_cast<int64_t>(kr) * a.key_stride_k;
+        c = pack_cand(tc_exact(a.qlow + t * a.l, kp, a.l), a.idx_offset + static_cast<uint32_t>(kr));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) {
+    const unsigned long long oc = __shfl_xor_sync(0xffffffffu, c, o);
+    c = oc > c ? oc : c;
+  }
+  if (i == 0 && c) atomicMax(reinterpret_cast<unsigned long long*>(a.best + p), c);
 }
 
 }  // namespace alut

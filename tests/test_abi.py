@@ -115,3 +115,20 @@ def test_integration_stub_matches_the_binding(stub, ours):
     a, b = _integration_stub_structs()[stub], getattr(_alut, ours)
     assert ctypes.sizeof(a) == ctypes.sizeof(b)
     assert [(n, getattr(a, n).offset) for n, _ in a._fields_] == [(n, getattr(b, n).offset) for n, _ in b._fields_]
+
+
+def test_scan_kind_follows_the_measured_crossovers():
+    """alut_scan_kind is a host-side rule (no GPU): decode chain up to 32 tokens / 256 slots,
+    tensor-core scan from 512 slots with >= 12 slots per routed table, else CUDA-core."""
+    lib = _alut.load()
+    t, _ = _tables(E=128, K=1024, L=64, H=256)
+    assert lib.alut_scan_kind(t, 16, 8) == _alut.SCAN_DECODE
+    assert lib.alut_scan_kind(t, 64, 8) == _alut.SCAN_CUDA_CORE      # 2 slots per table
+    assert lib.alut_scan_kind(t, 512, 8) == _alut.SCAN_TENSOR_CORE   # 16 per table
+    assert lib.alut_scan_kind(t, 4096, 8) == _alut.SCAN_TENSOR_CORE
+    t96, _ = _tables(E=72, K=2048, L=96, H=256)
+    assert lib.alut_scan_kind(t96, 8, 6) == _alut.SCAN_DECODE
+    assert lib.alut_scan_kind(t96, 2048, 6) == _alut.SCAN_TENSOR_CORE
+    t12, _ = _tables(E=4, K=100, L=12, H=256)  # L % 16 != 0: never the tensor cores
+    assert lib.alut_scan_kind(t12, 4096, 8) == _alut.SCAN_CUDA_CORE
+    assert lib.alut_scan_kind(None, 1, 1) < 0
