@@ -59,9 +59,11 @@ class LookupStepGraph:
                      ("compute", (q, s), torch.bool)]
         # Byte layout of the two arenas: per layer, each field at a 256-byte boundary.
         plan, off_in, off_out = [], 0, 0
+        self._in_ranges, self._out_ranges = [], []  # per-layer [start, stop) of each arena
         for eng in self.engines:
             h = eng.manager.values_buffer.shape[-1]
             fields = {}
+            in0, out0 = off_in, off_out
             for name, shape, dt in in_fields:
                 shape = shape or (q, h)
                 fields[name] = ("in", off_in, shape, dt)
@@ -70,6 +72,8 @@ class LookupStepGraph:
             fields["out"] = ("out", off_out, (q, h), vdt)
             off_out = (off_out + _nbytes((q, h), vdt) + 255) // 256 * 256
             plan.append(fields)
+            self._in_ranges.append((in0, off_in))
+            self._out_ranges.append((out0, off_out))
         self.in_dev = torch.zeros(off_in, dtype=torch.uint8, device=self.device)
         self.out_dev = torch.zeros(off_out, dtype=torch.uint8, device=self.device)
         self.in_host = torch.zeros(off_in, dtype=torch.uint8, pin_memory=True)
@@ -110,15 +114,54 @@ class LookupStepGraph:
             if not self.accumulate:
                 b.out.copy_(out)
 
+    def _step_with_copies(self, lib):
+        """Inputs in two copies (the first layers' alone, so that the first lookup starts
+        early; the rest while it runs), outputs in three (after about half of the layers,
+        after about 85%, and the rest), all on a second stream. The lookups wait only at the
+        two input boundaries, so programmatic launch still chains the other layers."""
+        main = torch.cuda.current_stream(self.device)
+        copy = torch.cuda.Stream(self.device)
+        copy.wait_stream(main)
+        n = len(self.engines)
+        in_cuts = sorted({0, min(2, n), n})
+        out_cuts = sorted({0, max(1, n // 2), max(1, (n * 85) // 100), n})
+        landed = {}
+        with torch.cuda.stream(copy):
+            for lo, hi in zip(in_cuts, in_cuts[1:]):
+                a, b = self._in_ranges[lo][0], self._in_ranges[hi - 1][1]
+                self.in_dev[a:b].copy_(self.in_host[a:b], non_blocking=True)
+                landed[lo] = torch.cuda.Event()
+                landed[lo].record(copy)
+        for i, (eng, b) in enumerate(zip(self.engines, self.layers)):
+            if i in landed:
+                main.wait_event(landed[i])
+            out = eng.lookup_combine(b.x, b.sel, b.is_vision, b.reuse, b.weights, compute_mask=b.compute,
+                                     out=b.out if self.accumulate else None, variant=self.variant,
+                                     renorm=self.renorm,
+                                     hit_out=None if self.hits is None else self.hits[i],
+                                     idx_out=None if self.idx is None else self.idx[i])
+            if not self.accumulate:
+                b.out.copy_(out)
+            if i + 1 in out_cuts:
+                lo = out_cuts[out_cuts.index(i + 1) - 1]
+                done = torch.cuda.Event()
+                done.record(main)
+                copy.wait_event(done)
+                with torch.cuda.stream(copy):
+                    a, b2 = self._out_ranges[lo][0], self._out_ranges[i][1]
+                    self.out_host[a:b2].copy_(self.out_dev[a:b2], non_blocking=True)
+        main.wait_stream(copy)
+
     def run_eager(self):
         """Issue the per-layer fused lookups on the current stream (no graph)."""
         self._step(None, _alut.load())
 
     def capture(self, *, with_copies=False, profile_events=None, warmup=2):
-        """Capture one step. ``with_copies`` adds the host->device copy of all inputs before
-        and the device->host copy of all outputs after the lookups. ``profile_events`` (one
-        (start, stop) pair of timing events per layer, already recorded once so that they
-        exist) brackets each layer's centroid-scan kernel inside the graph."""
+        """Capture one step. ``with_copies`` adds the host->device copy of the layers' inputs
+        and the device->host copy of their outputs, on a second stream, overlapping the
+        lookups (see ``_step_with_copies``).
+        ``profile_events`` (one (start, stop) pair of timing events per layer, already
+        recorded once so that they exist) brackets each layer's centroid-scan kernel."""
         if profile_events is not None and len(profile_events) != len(self.engines):
             raise ValueError("one (start, stop) event pair per layer")
         lib = _alut.load()
@@ -133,10 +176,9 @@ class LookupStepGraph:
         try:
             with torch.cuda.graph(self.graph):
                 if with_copies:
-                    self.in_dev.copy_(self.in_host, non_blocking=True)
-                self._step(profile_events, lib)
-                if with_copies:
-                    self.out_host.copy_(self.out_dev, non_blocking=True)
+                    self._step_with_copies(lib)
+                else:
+                    self._step(profile_events, lib)
         finally:
             lib.alut_set_profile_events(None, None)
         self.with_copies = with_copies

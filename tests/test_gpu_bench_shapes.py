@@ -142,3 +142,29 @@ def test_bad_expert_ids_raise_with_error_checks(Q, S):
     keep[Q // 2, S - 1] = False
     assert torch.equal(h0[keep], h1[keep]) and torch.equal(i0[keep], i1[keep])
     assert eng.device_errors() & 1
+
+
+def test_step_graph_with_overlapped_copies_matches_device_graph():
+    """The end-to-end graph (per-layer host->device input copies and device->host output
+    copies on a second stream, overlapping the other layers) gives the device graph's
+    outputs in host memory."""
+    from table_moe.cache_engine.step_graph import LookupStepGraph
+
+    layers = (0, 1, 2)
+    mgrs = [bench.build_layer(li, DEV, 0) for li in layers]
+    inputs = [bench.layer_inputs(li, 0) for li in layers]
+    engines = [VectorSearchEngine(m) for m in mgrs]
+    dev = LookupStepGraph(engines, bench.CFG["tokens"], bench.CFG["top_k"], variant="decode", accumulate=False)
+    e2e = LookupStepGraph(engines, bench.CFG["tokens"], bench.CFG["top_k"], variant="decode", accumulate=False)
+    for b, hb, inp in zip(dev.layers, e2e.host_layers, inputs):
+        for name, t in inp.items():
+            getattr(b, name).copy_(t)
+            getattr(hb, name).copy_(t)
+    dev.capture()
+    e2e.capture(with_copies=True)
+    for _ in range(2):
+        dev.replay()
+        e2e.replay()
+    torch.cuda.synchronize()
+    for b, hb in zip(dev.layers, e2e.host_layers):
+        assert torch.equal(b.out.cpu().view(torch.int16), hb.out.view(torch.int16))
