@@ -116,15 +116,16 @@ class LookupStepGraph:
 
     def _step_with_copies(self, lib):
         """Inputs in two copies (the first layers' alone, so that the first lookup starts
-        early; the rest while it runs), outputs in three (after about half of the layers,
-        after about 85%, and the rest), all on a second stream. The lookups wait only at the
-        two input boundaries, so programmatic launch still chains the other layers."""
+        early; the rest while it runs), outputs every four layers and the last layer's alone
+        (so that little is left to copy after the last lookup), all on a second stream. The
+        lookups wait only at the two input boundaries, so programmatic launch still chains
+        the other layers."""
         main = torch.cuda.current_stream(self.device)
         copy = torch.cuda.Stream(self.device)
         copy.wait_stream(main)
         n = len(self.engines)
         in_cuts = sorted({0, min(2, n), n})
-        out_cuts = sorted({0, max(1, n // 2), max(1, (n * 85) // 100), n})
+        out_cuts = sorted(set(range(0, n, 4)) | {max(0, n - 1), n})
         landed = {}
         with torch.cuda.stream(copy):
             for lo, hi in zip(in_cuts, in_cuts[1:]):
