@@ -583,7 +583,7 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a
 }
 
 constexpr int kMmaKBlock = 8;             // k-steps whose fragments are loaded together
-constexpr size_t kMmaStageBudget = 160 * 1024;  // shared memory for a staged basis slice
+constexpr size_t kMmaStageBudget = 200 * 1024;  // shared memory for a staged basis slice (L=96, H=2560 fits)
 
 // Shared memory of k_project_mma: the CTA's slice of the split basis (both modalities,
 // 3 parts, L columns, rows of krange k padded by 16 bytes so fragment loads of 8 columns
