@@ -318,7 +318,7 @@ static int launch_project(int key_dtype, int x_dtype, const ProjPlanArgs& a, cud
     // The cluster size may drop to 8 inside launch_project_kernel; size for the larger layout.
     const size_t sm = std::max(mma_smem_layout(a.l, a.h, a.nsplit).total,
                                mma_smem_layout(a.l, a.h, std::min(a.nsplit, 8)).total);
-    return launch_project_kernel(k_project_mma<float>, a, sm, st);
+    return launch_project_kernel(a.l <= 64 ? k_project_mma<float, 1> : k_project_mma<float, 2>, a, sm, st);
   }
   switch (key_dtype) {
     case ALUT_F32: return launch_project_k<float>(x_dtype, a, smem, st);

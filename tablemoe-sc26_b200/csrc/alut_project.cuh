@@ -607,7 +607,10 @@ __host__ __device__ inline MmaSmem mma_smem_layout(int l, int h, int nsplit) {
   return m;
 }
 
-template <typename TK>
+// NT: n-tiles a warp takes per pass (1 when L <= 64, 2 above): the register footprint of the
+// common L = 64 case stays that of one tile, which keeps room on the SMs for the CTAs of the
+// kernels around it.
+template <typename TK, int NT>
 __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   extern __shared__ __align__(256) unsigned char psm[];
   ALUT_TRACE(0);
@@ -689,10 +692,14 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
   // arrive now, wait just before the first remote store (the MMAs run in between).
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   bool cluster_ready = false;
-  for (int nt = warp; nt < ntiles; nt += kProjThreads / 32) {
-    // One accumulator per basis part: three independent MMA chains, added (hi + mid) + lo
-    // at the end.
-    float cp[3][4] = {};
+  // A warp owns n-tiles warp, warp + 8, ...; it takes them NT at a time so that one load of
+  // its x fragments serves them all.
+  constexpr int kWarps = kProjThreads / 32;
+  for (int nt0 = warp; nt0 < ntiles; nt0 += NT * kWarps) {
+    const int nts = (NT == 2 && nt0 + kWarps < ntiles) ? 2 : 1;
+    // One accumulator per (n-tile, basis part): independent MMA chains, each n-tile's parts
+    // added (hi + mid) + lo at the end.
+    float cp[NT][3][4] = {};
     for (int kb = k_begin; kb < k_end; kb += kMmaKBlock) {
       const int kn = min(kMmaKBlock, k_end - kb);
       if (kb != x_block) {
@@ -710,40 +717,52 @@ __global__ void __launch_bounds__(kProjThreads) k_project_mma(ProjPlanArgs a) {
             const uint32_t am[4] = {xa[s][0] & keep0, xa[s][1] & keep1, xa[s][2] & keep0, xa[s][3] & keep1};
             const int kl = (kb + s - k_begin) * 16 + 2 * tq;  // k within the slice
 #pragma unroll
-            for (int part = 0; part < 3; ++part) {
-              const int row = (m * 3 + part) * L + nt * 8 + gq;
-              uint32_t b0, b1;
-              if (lay.staged) {
-                const unsigned char* br = psm + static_cast<size_t>(row) * lay.pitch;
-                b0 = *reinterpret_cast<const uint32_t*>(br + kl * 2);
-                b1 = *reinterpret_cast<const uint32_t*>(br + kl * 2 + 16);
-              } else {
-                const __nv_bfloat16* bg = a.proj_split + static_cast<int64_t>(row) * H + static_cast<int64_t>(k_begin) * 16 + kl;
-                b0 = *reinterpret_cast<const uint32_t*>(bg);
-                b1 = *reinterpret_cast<const uint32_t*>(bg + 8);
+            for (int t = 0; t < NT; ++t) {
+              if (t < nts) {
+#pragma unroll
+                for (int part = 0; part < 3; ++part) {
+                  const int row = (m * 3 + part) * L + (nt0 + t * kWarps) * 8 + gq;
+                  uint32_t b0, b1;
+                  if (lay.staged) {
+                    const unsigned char* br = psm + static_cast<size_t>(row) * lay.pitch;
+                    b0 = *reinterpret_cast<const uint32_t*>(br + kl * 2);
+                    b1 = *reinterpret_cast<const uint32_t*>(br + kl * 2 + 16);
+                  } else {
+                    const __nv_bfloat16* bg =
+                        a.proj_split + static_cast<int64_t>(row) * H + static_cast<int64_t>(k_begin) * 16 + kl;
+                    b0 = *reinterpret_cast<const uint32_t*>(bg);
+                    b1 = *reinterpret_cast<const uint32_t*>(bg + 8);
+                  }
+                  mma_bf16_16816(cp[t][part], am, b0, b1);
+                }
               }
-              mma_bf16_16816(cp[part], am, b0, b1);
             }
           }
         }
       }
     }
-    float c[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) c[i] = (cp[0][i] + cp[1][i]) + cp[2][i];
     // Push the partial rows to their owners' receive buffers (slot = this rank).
     if (!cluster_ready) {
       asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
       cluster_ready = true;
     }
-    const int col = nt * 8 + 2 * tq;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int r = gq + 8 * half;
-      const int owner = r / rows_per;
-      float* dst = cluster.map_shared_rank(recv, owner) + (static_cast<size_t>(sp) * rows_per + r % rows_per) * L + col;
-      dst[0] = c[2 * half];
-      dst[1] = c[2 * half + 1];
+    for (int t = 0; t < NT; ++t) {
+      if (t < nts) {
+        float c[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c[i] = (cp[t][0][i] + cp[t][1][i]) + cp[t][2][i];
+        const int col = (nt0 + t * kWarps) * 8 + 2 * tq;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int r = gq + 8 * half;
+          const int owner = r / rows_per;
+          float* dst =
+              cluster.map_shared_rank(recv, owner) + (static_cast<size_t>(sp) * rows_per + r % rows_per) * L + col;
+          dst[0] = c[2 * half];
+          dst[1] = c[2 * half + 1];
+        }
+      }
     }
   }
   if (!cluster_ready) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // warps without n-tiles
