@@ -341,16 +341,23 @@ __device__ __noinline__ int tc_make_room(int e, float thr, const float* q, const
   return 0;
 }
 
-// Maximum of 32 values as a depth-5 tree (independent operations, no serial chain).
+// Three-input maximum (sm_100 max.f32 with three operands; NaN handling as fmaxf).
+__device__ __forceinline__ float tc_max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Maximum of 32 values as a tree of three-input maxima: 17 operations (32 -> 11 -> 4 -> 2
+// -> 1), all independent within a level.
 __device__ __forceinline__ float tc_max32(const float (&v)[32]) {
-  float m[16];
+  float m[11];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) m[j] = fmaxf(v[j], v[j + 16]);
-#pragma unroll
-  for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-    for (int j = 0; j < w; ++j) m[j] = fmaxf(m[j], m[j + w]);
-  return m[0];
+  for (int j = 0; j < 10; ++j) m[j] = tc_max3(v[3 * j], v[3 * j + 1], v[3 * j + 2]);
+  m[10] = fmaxf(v[30], v[31]);
+  const float n0 = tc_max3(m[0], m[1], m[2]), n1 = tc_max3(m[3], m[4], m[5]), n2 = tc_max3(m[6], m[7], m[8]),
+              n3 = fmaxf(m[9], m[10]);
+  return fmaxf(tc_max3(n0, n1, n2), n3);
 }
 
 // ---- scan ------------------------------------------------------------------------------------
