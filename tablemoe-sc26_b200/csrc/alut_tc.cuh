@@ -19,16 +19,19 @@
 // table's largest row norm; the searched slots' queries are staged per search group in the
 // same order (k_stage_queries). One TMA bulk copy then brings a whole operand tile.
 //
-// Pipeline (one CTA per SM, persistent over a contiguous range of (group, chunk) tiles so
-// that a group's query tile is loaded once and its chunks stream in order):
-//   warp 8 (producer): query tile -> A[2], key chunk -> stage ring (mbarrier full/empty);
+// Pipeline (one CTA per SM, persistent over a contiguous range of (group, tile) pairs so
+// that a group's query tile is loaded once and its key tiles stream in order; a tile is
+// kTcCpt adjacent 128-row chunks, one MMA of N = 128 kTcCpt centroids):
+//   warp 8 (producer): query tile -> A[2], a tile's chunks (one bulk copy) -> stage ring
+//                 (mbarrier full/empty);
 //   warp 9 (MMA): allocates all 512 TMEM columns, issues L/16 MMAs per tile into one of
-//                 four 128-column fp32 accumulators, commits to the stage's `empty`, the
+//                 kTcAcc fp32 128 x N accumulators, commits to the stage's `empty`, the
 //                 accumulator's `full` and, at a group's last tile, the query buffer's
 //                 `empty` barrier;
 //   warps 0-7 (epilogue): warp w reads TMEM lane quarter w % 4 (slots 32 (w % 4)..) over
-//                 centroid columns 64 (w / 4).. of the tile, releases the accumulator,
-//                 filters candidates and rescores them at the group's end.
+//                 column half w / 4 of the tile, 64 columns per load, releases the
+//                 accumulator after its last load, filters candidates and hands the
+//                 survivors to the exact rescoring at the group's end.
 // Every wait is bounded in time; on expiry the CTA records an error bit, stops all roles,
 // drains what it has in flight (bounded), frees TMEM and returns.
 #pragma once
@@ -60,8 +63,16 @@ inline bool tc_scan_wanted(int64_t slots, int num_tables) {
 }
 constexpr int kTcCand = 8;          // candidate list per (slot, column half)
 constexpr int kTcMaxStages = 8;
-constexpr int kTcAcc = 4;                          // fp32 128x128 accumulators in TMEM
-constexpr uint32_t kTcTmemCols = kTcAcc * kTcRows;  // all 512 columns: one CTA per SM
+// 128-row key chunks per tile: one MMA covers N = 128 * kTcCpt centroids, so the query
+// operand is read from shared memory once per kTcCpt chunks.
+#ifndef ALUT_TC_CPT
+#define ALUT_TC_CPT 2
+#endif
+constexpr int kTcCpt = ALUT_TC_CPT;
+static_assert(kTcCpt == 1 || kTcCpt == 2, "MMA N of 128 or 256");
+constexpr int kTcN = kTcRows * kTcCpt;              // centroids per tile (MMA N)
+constexpr uint32_t kTcTmemCols = 512;               // all of tensor memory: one CTA per SM
+constexpr int kTcAcc = kTcTmemCols / kTcN;          // fp32 128 x N accumulators (4 or 2)
 constexpr size_t kTcSmemBudget = 212 * 1024;
 
 // Byte offset of element (row, k) in a [rows][L] bf16 operand in the K-major, no-swizzle
@@ -73,13 +84,15 @@ __host__ __device__ __forceinline__ uint32_t tc_off(int r, int k, int L) {
 
 // One operand tile: 128 rows x L bf16.
 __host__ __device__ inline size_t tc_tile_bytes(int l) { return static_cast<size_t>(kTcRows) * l * 2; }
+// Key stages of kTcCpt chunks each, in the shared memory left after the two query tiles
+// and the candidate lists.
 inline int tc_stages(int l) {
   const size_t t = tc_tile_bytes(l);
-  const size_t n = (kTcSmemBudget - 1024 - 2 * t - sizeof(float) * 2 * kTcCand * kTcEpiThreads) / t;
+  const size_t n = (kTcSmemBudget - 1024 - 2 * t - sizeof(float) * 2 * kTcCand * kTcEpiThreads) / (kTcCpt * t);
   return static_cast<int>(n < kTcMaxStages ? n : kTcMaxStages);
 }
 inline size_t search_tc_smem_bytes(int l) {
-  return 1024 + (2 + static_cast<size_t>(tc_stages(l))) * tc_tile_bytes(l) +
+  return 1024 + (2 + static_cast<size_t>(kTcCpt) * tc_stages(l)) * tc_tile_bytes(l) +
          sizeof(float) * 2 * kTcCand * kTcEpiThreads;
 }
 // Upper bound of the search groups of the tensor-core plan (groups of <= 128 slots of one table).
@@ -206,9 +219,9 @@ __device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, int L) {
   d |= static_cast<uint64_t>(1) << 46;                                                  // descriptor version
   return d;                                                                             // no swizzle
 }
-// kind::f16 instruction descriptor: fp32 D, bf16 A and B, both K-major, M = N = 128.
+// kind::f16 instruction descriptor: fp32 D, bf16 A and B, both K-major, M = 128, N = kTcN.
 __host__ __device__ __forceinline__ uint32_t tc_idesc() {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kTcRows >> 3) << 17) |
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kTcN >> 3) << 17) |
          (static_cast<uint32_t>(kTcRows >> 4) << 24);
 }
 __device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t acc) {
@@ -421,8 +434,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
   uint64_t* t_empty = t_full + kTcAcc;                // [kTcAcc]
   uint64_t* drain = t_empty + kTcAcc;                 // [1]
   unsigned char* sA = tsm + 1024;                     // [2][tile]
-  unsigned char* sK = sA + 2 * tb;                    // [NS][tile]
-  int* s_cc = reinterpret_cast<int*>(sK + static_cast<size_t>(NS) * tb);  // [kTcCand][256]
+  unsigned char* sK = sA + 2 * tb;                    // [NS][kTcCpt tiles]
+  int* s_cc = reinterpret_cast<int*>(sK + static_cast<size_t>(NS) * kTcCpt * tb);  // [kTcCand][256]
   float* s_cv = reinterpret_cast<float*>(s_cc + kTcCand * kTcEpiThreads);  // [kTcCand][256]
   __shared__ unsigned long long s_mine[kTcEpiThreads];  // best exactly rescored candidate
   __shared__ uint32_t s_tmem;
@@ -431,7 +444,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
   volatile int* abort_flag = &s_abort;
   TC_TRACE_DECL;
 
-  const int ntiles = a.meta[0] * a.nchunks;
+  const int nt = (a.nchunks + kTcCpt - 1) / kTcCpt;  // tiles per group
+  const int ntiles = a.meta[0] * nt;
   const int t_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * ntiles / gridDim.x);
   const int t_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * ntiles / gridDim.x);
   if (t_begin >= t_end) return;
@@ -469,7 +483,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
     // ---- producer --------------------------------------------------------------------------
     if (lane == 0) {
       int gi = -1, prev = -1, it = 0, table = 0;
-      int g = t_begin / a.nchunks, c = t_begin - g * a.nchunks;  // advanced without divisions
+      int g = t_begin / nt, c = t_begin - g * nt;  // advanced without divisions
       int st = 0, wrapped = 0;                                      // stage, and its reuse parity
       bool ok = true;
       for (int tile = t_begin; tile < t_end && ok; ++tile, ++it) {
@@ -495,13 +509,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
           ok = false;
           break;
         }
-        mbar_expect_tx(&full[st], tb);
-        bulk_g2s(sK + st * tb, a.ksplit + (static_cast<int64_t>(table) * a.nchunks + c) * tb, tb, &full[st]);
+        // The tile's chunks are adjacent in the prepared form: one copy (the last tile of an
+        // odd chunk count brings one chunk; the MMA's other half reads columns masked later).
+        const uint32_t kbytes = static_cast<uint32_t>(min(kTcCpt, a.nchunks - c * kTcCpt)) * tb;
+        mbar_expect_tx(&full[st], kbytes);
+        bulk_g2s(sK + st * kTcCpt * tb, a.ksplit + (static_cast<int64_t>(table) * a.nchunks + c * kTcCpt) * tb, kbytes,
+                 &full[st]);
         if (++st == NS) {
           st = 0;
           wrapped ^= 1;
         }
-        if (++c == a.nchunks) {
+        if (++c == nt) {
           c = 0;
           ++g;
         }
@@ -517,7 +535,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
     // ---- MMA issuer ------------------------------------------------------------------------
     if (lane == 0) {
       int gi = -1, prev = -1, it = 0;
-      int g = t_begin / a.nchunks, c = t_begin - g * a.nchunks;
+      int g = t_begin / nt, c = t_begin - g * nt;
       int st = 0, sph = 0;  // stage and the parity of its current use
       bool ok = true;
       for (int tile = t_begin; tile < t_end; ++tile, ++it) {
@@ -546,8 +564,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
           break;
         }
         tc_fence_after();
-        const uint32_t a0 = smem_addr(sA + (gi & 1) * tb), b0 = smem_addr(sK + st * tb);
-        const uint32_t d = tmem + static_cast<uint32_t>(acc * kTcRows);
+        const uint32_t a0 = smem_addr(sA + (gi & 1) * tb), b0 = smem_addr(sK + st * kTcCpt * tb);
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * kTcN);
         if (L == 128) {
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) tc_mma(d, tc_desc(a0 + ks * 256, 128), tc_desc(b0 + ks * 256, 128), ks > 0);
@@ -559,12 +577,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
         }
         tc_commit(&empty[st]);
         tc_commit(&t_full[acc]);
-        if (tile + 1 == t_end || c == a.nchunks - 1) tc_commit(&a_empty[gi & 1]);
+        if (tile + 1 == t_end || c == nt - 1) tc_commit(&a_empty[gi & 1]);
         if (++st == NS) {
           st = 0;
           sph ^= 1;
         }
-        if (++c == a.nchunks) {
+        if (++c == nt) {
           c = 0;
           ++g;
         }
@@ -575,8 +593,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       }
     }
   } else {
-    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. (slots), columns 64 (w / 4) ..
-    // (centroids); thread e keeps the running maximum and candidates of its (slot, half).
+    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. (slots) over the column half
+    // w / 4 of the tile (centroids), 64 columns per load; thread e keeps the running maximum
+    // and candidates of its (slot, half).
     const int e = tid;
     const int r = (warp & 3) * 32 + lane;
     const int half = warp >> 2;
@@ -585,8 +604,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
     float amax = -INFINITY, tw = 0.f;
     const float* q = nullptr;
     const float* kt = nullptr;
-    int g = t_begin / a.nchunks, c = t_begin - g * a.nchunks;
-    for (int tile = t_begin; tile < t_end; ++tile, ++it, (++c == a.nchunks ? (c = 0, ++g) : 0)) {
+    int g = t_begin / nt, c = t_begin - g * nt;
+    for (int tile = t_begin; tile < t_end; ++tile, ++it, (++c == nt ? (c = 0, ++g) : 0)) {
       if (g != prev) {
         prev = g;
         const int4 gg = a.groups[g];
@@ -619,21 +638,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
         break;
       }
       tc_fence_after();
-      float v[64];
-      {
+#pragma unroll
+      for (int sub = 0; sub < kTcCpt; ++sub) {
+        float v[64];
+        {
+          TC_T0();
+          __syncwarp();
+          tc_ld64(lane_base + static_cast<uint32_t>(acc * kTcN + half * (kTcN / 2) + sub * 64), v);
+          TC_ACC(41);
+        }
+        if (sub == kTcCpt - 1) {
+          // The accumulator may be overwritten as soon as every warp has its values.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&t_empty[acc]);
+        }
+        if (p < 0) continue;
         TC_T0();
-        __syncwarp();
-        tc_ld64(lane_base + static_cast<uint32_t>(acc * kTcRows + half * 64), v);
-        TC_ACC(41);
-      }
-      // The accumulator may be overwritten as soon as every warp has its values.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&t_empty[acc]);
-      if (p >= 0) {
-        TC_T0();
-        const int rows = min(kTcRows, a.k - c * kTcRows) - half * 64;  // valid columns of this half
-        const int kb = c * kTcRows + half * 64;
+        const int kb = c * kTcN + half * (kTcN / 2) + sub * 64;
+        const int rows = a.k - kb;  // valid columns of this block (<= 0: none)
         if (rows < 64) {
 #pragma unroll
           for (int j = 0; j < 64; ++j)
@@ -674,7 +697,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
           }
         }
         TC_ACC(43);
-        if (tile + 1 == t_end || c == a.nchunks - 1) {
+      }
+      if (p >= 0) {
+        if (tile + 1 == t_end || c == nt - 1) {
           // End of this CTA's part of the group: the surviving candidates go to the rescoring
           // pass (k_tc_rescore) instead of being rescored here, where each one would hold
           // the accumulators for a dependent global load; a full list rescored here.
