@@ -552,7 +552,7 @@ static int run_search(const alut_tables_t* t, const alut_batch_t* b, const alut_
     if (!q_direct) rc = launch_project(t->key_dtype, b->x_dtype, a, st);
     if (rc) return rc;
     const int ntab = 2 * t->num_experts;
-    const int nchunks = ceil_div(t->k, kTcRows);
+    const int nchunks = tc_prep_chunks(t->k);
     TcArgs c{};
     c.ksplit = static_cast<const unsigned char*>(ksplit);
     c.knorm = reinterpret_cast<const float*>(static_cast<const char*>(ksplit) +
@@ -978,7 +978,7 @@ size_t alut_keys_split_bytes(const alut_tables_t* t) {
       t->num_experts <= 0)
     return 0;
   const int64_t ntab = 2 * static_cast<int64_t>(t->num_experts);
-  const int64_t nchunks = (t->k + kTcRows - 1) / kTcRows;
+  const int64_t nchunks = tc_prep_chunks(t->k);
   return align256(ntab * nchunks * tc_tile_bytes(t->l)) + align256(sizeof(float) * ntab);
 }
 
@@ -989,7 +989,7 @@ int alut_prepare_keys(const alut_tables_t* t, int32_t keyset, void* out, size_t 
   const void* keys = keyset == ALUT_KEYS_RAW ? t->raw_keys : (keyset == ALUT_KEYS_NORMALISED ? t->keys : nullptr);
   if (!keys) return fail(ALUT_EINVAL, "prepare_keys: key set %d is NULL", keyset);
   const int ntab = 2 * t->num_experts;
-  const int nchunks = (t->k + kTcRows - 1) / kTcRows;
+  const int nchunks = tc_prep_chunks(t->k);
   const size_t body = align256(static_cast<size_t>(ntab) * nchunks * tc_tile_bytes(t->l));
   float* norms = reinterpret_cast<float*>(static_cast<char*>(out) + body);
   cudaError_t e = cudaMemsetAsync(norms, 0, sizeof(float) * ntab, reinterpret_cast<cudaStream_t>(stream));

@@ -43,9 +43,17 @@ namespace alut {
 
 constexpr int kTcRows = 128;        // slots per tile (MMA M) and centroids per chunk (MMA N)
 constexpr int kTcMaxL = 128;
-constexpr int kTcEpiThreads = 256;  // warps 0-7: (TMEM lane quarter, column half)
-constexpr int kTcThreads = 320;     // + producer warp 8 + MMA warp 9
-constexpr int kTcProducerWarp = 8, kTcMmaWarp = 9;
+// Epilogue warps 0 .. kTcEpiWarps-1: (TMEM lane quarter, column part); then the producer
+// warp and the MMA warp.
+#ifndef ALUT_TC_EPI_WARPS
+#define ALUT_TC_EPI_WARPS 8
+#endif
+constexpr int kTcEpiWarps = ALUT_TC_EPI_WARPS;
+static_assert(kTcEpiWarps == 8 || kTcEpiWarps == 16, "two or four column parts");
+constexpr int kTcColParts = kTcEpiWarps / 4;
+constexpr int kTcEpiThreads = 32 * kTcEpiWarps;
+constexpr int kTcThreads = kTcEpiThreads + 64;
+constexpr int kTcProducerWarp = kTcEpiWarps, kTcMmaWarp = kTcEpiWarps + 1;
 #ifndef ALUT_TC_MIN_PAIRS
 #define ALUT_TC_MIN_PAIRS 512
 #endif
@@ -61,7 +69,7 @@ inline bool tc_scan_wanted(int64_t slots, int num_tables) {
   const int64_t tables = slots < num_tables ? slots : num_tables;
   return slots >= kTcMinPairs && slots >= kTcMinSlotsPerTable * tables;
 }
-constexpr int kTcCand = 8;          // candidate list per (slot, column half)
+constexpr int kTcCand = 64 / kTcEpiWarps;  // candidate list per (slot, column part)
 constexpr int kTcMaxStages = 8;
 // 128-row key chunks per tile: one MMA covers N = 128 * kTcCpt centroids, so the query
 // operand is read from shared memory once per kTcCpt chunks.
@@ -80,6 +88,14 @@ constexpr size_t kTcSmemBudget = 212 * 1024;
 // groups L*16 bytes apart.
 __host__ __device__ __forceinline__ uint32_t tc_off(int r, int k, int L) {
   return static_cast<uint32_t>((r >> 3) * (L * 16) + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
+}
+
+// 128-row chunks per table in the prepared key form: ceil(K / 128) rounded up to whole
+// tiles. Rows past K are NaN: their scores are NaN, which max.f32 ignores and which no
+// >= comparison accepts, so the scan needs no column mask.
+__host__ __device__ inline int tc_prep_chunks(int k) {
+  const int c = (k + kTcRows - 1) / kTcRows;
+  return (c + kTcCpt - 1) / kTcCpt * kTcCpt;
 }
 
 // One operand tile: 128 rows x L bf16.
@@ -102,7 +118,8 @@ __host__ __device__ inline int64_t tc_max_groups(int64_t pairs, int ntab) {
 
 // ---- preparation ---------------------------------------------------------------------------
 
-// out: [tables][nchunks][128 x L bf16 core-matrix order], then float norms[tables].
+// out: [tables][nchunks = tc_prep_chunks(K)][128 x L bf16 core-matrix order], then float
+// norms[tables].
 // One thread per (table, chunk, row, 8 columns): eight reads, one 16-byte store.
 __global__ void k_prepare_keys(const float* keys, int64_t se, int64_t sm, int64_t sk, int ntab, int K, int L,
                                int nchunks, __nv_bfloat16* out, float* norms) {
@@ -117,7 +134,9 @@ __global__ void k_prepare_keys(const float* keys, int64_t se, int64_t sm, int64_
     const int c = static_cast<int>(tcn % nchunks);
     const int t = static_cast<int>(tcn / nchunks);
     const int kr = c * kTcRows + r;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __int_as_float(0x7fc00000);  // NaN rows past K
     if (kr < K) {
       const float* src = keys + static_cast<int64_t>(t >> 1) * se + static_cast<int64_t>(t & 1) * sm +
                          static_cast<int64_t>(kr) * sk + u * 8;
@@ -281,6 +300,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// An epilogue warp is done reading an accumulator (all its loads waited for): one arrival,
+// after which the MMA warp may overwrite it.
+__device__ __forceinline__ void tc_release(uint64_t* t_empty, int lane) {
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(t_empty);
+}
+
 // Bounded wait that also gives up when another role of the CTA has aborted.
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;  // the common case: no timer read
@@ -373,6 +400,43 @@ __device__ __forceinline__ float tc_max32(const float (&v)[32]) {
   return fmaxf(tc_max3(n0, n1, n2), n3);
 }
 
+// Bit j set where v[j] >= thr, built as a balanced tree of ORs (depth 5, not a chain of 32).
+__device__ __forceinline__ uint32_t tc_mask32(const float (&v)[32], float thr) {
+  uint32_t b[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) b[j] = (v[j] >= thr ? 1u : 0u) << j;
+#pragma unroll
+  for (int w = 16; w > 0; w >>= 1)
+#pragma unroll
+    for (int j = 0; j < w; ++j) b[j] |= b[j + w];
+  return b[0];
+}
+
+// The (group, tile) items a CTA walks over its range [t_begin, t_end) of group-major tile
+// indices, in the same order in every role, without divisions; a segment is the CTA's part
+// of one group.
+struct TcWalk {
+  int nt, glast, cend_last;
+  int g, c, ce;  // group, tile, end of the segment
+  __device__ __forceinline__ void begin(int t_begin, int t_end, int nt_) {
+    nt = nt_;
+    g = t_begin / nt;
+    c = t_begin - g * nt;
+    glast = (t_end - 1) / nt;
+    cend_last = t_end - glast * nt;
+    ce = g == glast ? cend_last : nt;
+  }
+  __device__ __forceinline__ bool done() const { return g > glast; }
+  __device__ __forceinline__ bool segment_end() const { return c == ce - 1; }
+  __device__ __forceinline__ void next() {
+    if (++c == ce) {
+      ++g;
+      c = 0;
+      ce = g == glast ? cend_last : nt;
+    }
+  }
+};
+
 // ---- scan ------------------------------------------------------------------------------------
 
 struct TcArgs {
@@ -397,12 +461,15 @@ struct TcArgs {
 #ifdef ALUT_PHASE_TRACE
 // Development builds: per-thread SM-cycle sums kept in registers (slots 40..55), written once
 // at the end by block 0's epilogue thread 0 (40 accumulator wait, 41 TMEM load, 42 group-end
-// rescoring, 43 filter, 45 slow-path tiles, 46 list overflows, 48 rescored centroids), MMA
-// thread (50 stage wait, 51 accumulator wait) and producer thread (52 stage wait).
+// rescoring, 43 filter, 45 slow-path tiles, 46 list overflows, 48 rescored centroids, 53 the
+// whole tile loop, 54 kernel entry to exit), MMA thread (50 stage wait, 51 accumulator wait)
+// and producer thread (52 stage wait).
 #define TC_TRACE_DECL unsigned long long tc_tr_[16] = {}
 #define TC_T0() const long long tc_t0_ = clock64()
 #define TC_ACC(slot) tc_tr_[(slot) - 40] += static_cast<unsigned long long>(clock64() - tc_t0_)
 #define TC_COUNT() tc_tr_[8] += 1
+#define TC_MARK(name) const long long name = clock64()
+#define TC_SINCE(name, slot) tc_tr_[(slot) - 40] += static_cast<unsigned long long>(clock64() - name)
 #define TC_T0_TID(t) TC_T0()
 #define TC_ACC_TID(t, slot) TC_ACC(slot)
 #define TC_INC_TID(t, slot) tc_tr_[(slot) - 40] += 1
@@ -415,6 +482,8 @@ struct TcArgs {
 #define TC_T0() do {} while (0)
 #define TC_ACC(slot) do {} while (0)
 #define TC_COUNT() do {} while (0)
+#define TC_MARK(name) do {} while (0)
+#define TC_SINCE(name, slot) do {} while (0)
 #define TC_T0_TID(t) do {} while (0)
 #define TC_ACC_TID(t, slot) do {} while (0)
 #define TC_INC_TID(t, slot) do {} while (0)
@@ -435,16 +504,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
   uint64_t* drain = t_empty + kTcAcc;                 // [1]
   unsigned char* sA = tsm + 1024;                     // [2][tile]
   unsigned char* sK = sA + 2 * tb;                    // [NS][kTcCpt tiles]
-  int* s_cc = reinterpret_cast<int*>(sK + static_cast<size_t>(NS) * kTcCpt * tb);  // [kTcCand][256]
-  float* s_cv = reinterpret_cast<float*>(s_cc + kTcCand * kTcEpiThreads);  // [kTcCand][256]
+  int* s_cc = reinterpret_cast<int*>(sK + static_cast<size_t>(NS) * kTcCpt * tb);  // [kTcCand][kTcEpiThreads]
+  float* s_cv = reinterpret_cast<float*>(s_cc + kTcCand * kTcEpiThreads);  // [kTcCand][kTcEpiThreads]
   __shared__ unsigned long long s_mine[kTcEpiThreads];  // best exactly rescored candidate
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_issued, s_groups_issued;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   volatile int* abort_flag = &s_abort;
   TC_TRACE_DECL;
+  TC_MARK(tc_entry_);
 
-  const int nt = (a.nchunks + kTcCpt - 1) / kTcCpt;  // tiles per group
+  const int nt = a.nchunks / kTcCpt;  // tiles per group (a.nchunks = tc_prep_chunks(K))
   const int ntiles = a.meta[0] * nt;
   const int t_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * ntiles / gridDim.x);
   const int t_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * ntiles / gridDim.x);
@@ -466,7 +536,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
     }
     for (int i = 0; i < kTcAcc; ++i) {
       mbar_init(&t_full[i], 1);
-      mbar_init(&t_empty[i], kTcEpiThreads / 32);  // one arrival per epilogue warp
+      mbar_init(&t_empty[i], kTcEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -483,10 +553,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
     // ---- producer --------------------------------------------------------------------------
     if (lane == 0) {
       int gi = -1, prev = -1, it = 0, table = 0;
-      int g = t_begin / nt, c = t_begin - g * nt;  // advanced without divisions
-      int st = 0, wrapped = 0;                                      // stage, and its reuse parity
+      int st = 0, wrapped = 0;  // stage, and its reuse parity
       bool ok = true;
-      for (int tile = t_begin; tile < t_end && ok; ++tile, ++it) {
+      TcWalk wk;
+      for (wk.begin(t_begin, t_end, nt); !wk.done() && ok; wk.next(), ++it) {
+        const int g = wk.g, c = wk.c;
         if (g != prev) {
           table = a.groups[g].x;
           const int ab = (gi + 1) & 1;
@@ -509,19 +580,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
           ok = false;
           break;
         }
-        // The tile's chunks are adjacent in the prepared form: one copy (the last tile of an
-        // odd chunk count brings one chunk; the MMA's other half reads columns masked later).
-        const uint32_t kbytes = static_cast<uint32_t>(min(kTcCpt, a.nchunks - c * kTcCpt)) * tb;
+        // The tile's chunks are adjacent in the prepared form (whole tiles): one copy.
+        const uint32_t kbytes = static_cast<uint32_t>(kTcCpt) * tb;
         mbar_expect_tx(&full[st], kbytes);
         bulk_g2s(sK + st * kTcCpt * tb, a.ksplit + (static_cast<int64_t>(table) * a.nchunks + c * kTcCpt) * tb, kbytes,
                  &full[st]);
         if (++st == NS) {
           st = 0;
           wrapped ^= 1;
-        }
-        if (++c == nt) {
-          c = 0;
-          ++g;
         }
       }
       s_issued = it;
@@ -535,10 +601,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
     // ---- MMA issuer ------------------------------------------------------------------------
     if (lane == 0) {
       int gi = -1, prev = -1, it = 0;
-      int g = t_begin / nt, c = t_begin - g * nt;
       int st = 0, sph = 0;  // stage and the parity of its current use
       bool ok = true;
-      for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+      TcWalk wk;
+      for (wk.begin(t_begin, t_end, nt); !wk.done(); wk.next(), ++it) {
+        const int g = wk.g;
         if (g != prev) {
           prev = g;
           ++gi;
@@ -577,14 +644,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
         }
         tc_commit(&empty[st]);
         tc_commit(&t_full[acc]);
-        if (tile + 1 == t_end || c == nt - 1) tc_commit(&a_empty[gi & 1]);
+        if (wk.segment_end()) tc_commit(&a_empty[gi & 1]);
         if (++st == NS) {
           st = 0;
           sph ^= 1;
-        }
-        if (++c == nt) {
-          c = 0;
-          ++g;
         }
       }
       if (!ok && !*abort_flag) {
@@ -593,19 +656,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       }
     }
   } else {
-    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. (slots) over the column half
+    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. (slots) over the column part
     // w / 4 of the tile (centroids), 64 columns per load; thread e keeps the running maximum
-    // and candidates of its (slot, half).
+    // and candidates of its (slot, part).
     const int e = tid;
     const int r = (warp & 3) * 32 + lane;
-    const int half = warp >> 2;
+    const int half = warp >> 2;  // column part
+    constexpr int kPartCols = kTcN / kTcColParts;
+    constexpr int kSubs = kPartCols / 64;  // 64-column loads per tile
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     int prev = -1, p = -1, n = 0, it = 0;
     float amax = -INFINITY, tw = 0.f;
     const float* q = nullptr;
     const float* kt = nullptr;
-    int g = t_begin / nt, c = t_begin - g * nt;
-    for (int tile = t_begin; tile < t_end; ++tile, ++it, (++c == nt ? (c = 0, ++g) : 0)) {
+    TC_MARK(tc_loop_);
+    TcWalk wk;
+    for (wk.begin(t_begin, t_end, nt); !wk.done(); wk.next(), ++it) {
+      const int g = wk.g, c = wk.c;
       if (g != prev) {
         prev = g;
         const int4 gg = a.groups[g];
@@ -639,51 +706,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       }
       tc_fence_after();
 #pragma unroll
-      for (int sub = 0; sub < kTcCpt; ++sub) {
+      for (int sub = 0; sub < kSubs; ++sub) {
         float v[64];
         {
           TC_T0();
           __syncwarp();
-          tc_ld64(lane_base + static_cast<uint32_t>(acc * kTcN + half * (kTcN / 2) + sub * 64), v);
+          tc_ld64(lane_base + static_cast<uint32_t>(acc * kTcN + half * kPartCols + sub * 64), v);
           TC_ACC(41);
         }
-        if (sub == kTcCpt - 1) {
-          // The accumulator may be overwritten as soon as every warp has its values.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&t_empty[acc]);
-        }
+        if (sub == kSubs - 1) tc_release(&t_empty[acc], lane);
         if (p < 0) continue;
         TC_T0();
-        const int kb = c * kTcN + half * (kTcN / 2) + sub * 64;
-        const int rows = a.k - kb;  // valid columns of this block (<= 0: none)
-        if (rows < 64) {
-#pragma unroll
-          for (int j = 0; j < 64; ++j)
-            if (j >= rows) v[j] = -INFINITY;
-        }
         const float m0 = tc_max32(*reinterpret_cast<const float(*)[32]>(v)),
                     m1 = tc_max32(*reinterpret_cast<const float(*)[32]>(v + 32));
-        // Masked columns (-inf) never qualify, even while amax is still -inf.
-        if (fmaxf(m0, m1) > -INFINITY && fmaxf(m0, m1) >= amax - tw) {  // rare once amax has settled
+        // Columns past K (NaN) never qualify: a block of them has NaN maxima, and every
+        // comparison with NaN is false, even while amax is still -inf.
+        if (fmaxf(m0, m1) >= amax - tw) {  // rare once amax has settled
           TC_INC_TID(0, 45);
           amax = fmaxf(amax, fmaxf(m0, m1));
           const float thr = amax - tw;
-          // Qualifying columns as bit masks (predicated compares, no branches), then one
-          // insertion per set bit - usually one.
-          uint32_t mk0 = 0u, mk1 = 0u;
-          if (m0 >= thr) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) mk0 |= (v[j] >= thr ? 1u : 0u) << j;
-          }
-          if (m1 >= thr) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) mk1 |= (v[32 + j] >= thr ? 1u : 0u) << j;
-          }
-          const uint64_t mk = (static_cast<uint64_t>(mk1) << 32) | mk0;
-          // The stored value: with one qualifying column it is the slice maximum itself; with
+          // Qualifying columns as bit masks, then one insertion per set bit - usually one.
+          const uint64_t mk =
+              (static_cast<uint64_t>(m1 >= thr ? tc_mask32(*reinterpret_cast<const float(*)[32]>(v + 32), thr) : 0u)
+               << 32) |
+              (m0 >= thr ? tc_mask32(*reinterpret_cast<const float(*)[32]>(v), thr) : 0u);
+          // The stored value: with one qualifying column it is the block maximum itself; with
           // several, amax - an upper bound, so pruning never drops a column that could win.
           const float x = __popcll(static_cast<long long>(mk)) == 1 ? fmaxf(m0, m1) : amax;
+          const int kb = c * kTcN + half * kPartCols + sub * 64;
           for (uint64_t m = mk; m; m &= m - 1) {
             const int j = __ffsll(static_cast<long long>(m)) - 1;
             if (n == kTcCand) {
@@ -693,13 +743,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
             s_cc[n * kTcEpiThreads + e] = kb + j;
             s_cv[n * kTcEpiThreads + e] = x;
             ++n;
-            tc_prefetch_row(kt + static_cast<int64_t>(kb + j) * a.key_stride_k, L);
           }
         }
         TC_ACC(43);
       }
       if (p >= 0) {
-        if (tile + 1 == t_end || c == nt - 1) {
+        if (wk.segment_end()) {
           // End of this CTA's part of the group: the surviving candidates go to the rescoring
           // pass (k_tc_rescore) instead of being rescored here, where each one would hold
           // the accumulators for a dependent global load; a full list rescored here.
@@ -723,6 +772,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
         }
       }
     }
+    if (tid == 0) TC_SINCE(tc_loop_, 53);
   }
 
   __syncthreads();
@@ -743,6 +793,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_search_tc(TcArgs a) {
       mbar_wait_bounded(&a_full[ab], (last >> 1) & 1);
     }
   }
+  if (tid == 0) TC_SINCE(tc_entry_, 54);
   TC_TRACE_FLUSH();
   __syncthreads();
   if (warp == kTcMmaWarp)
