@@ -581,25 +581,25 @@ def c4_workload(args, device, flush, peaks, checker):
 
 
 def c5_workload(args, rank, world, device, flush, peaks, checker):
-    """The large single table (K=65536, L=128 fp32 keys, 65536 x 4096 bf16 rows) sharded by
-    centroid range over the ranks; 32768 tokens (hidden 4096, bf16) looked up per step:
-    projection of this rank's tokens, NCCL all-gather of the queries, local tensor-core scan,
-    all-gather of packed candidates, merge, peer row gather; the step is one CUDA graph
-    (NCCL calls included). Strong scaling: the same tokens and table at every N."""
+    """The large single table (K=65536, L=128 fp32 keys, 65536 x 4096 bf16 rows): value rows
+    sharded by centroid range over the ranks, the 32 MiB key table replicated; 32768 tokens
+    (hidden 4096, bf16) looked up per step: each rank projects and scans (tensor cores) its own
+    Q/W tokens over the whole table, the packed winners are all-gathered (8 bytes a token) and
+    merged, and each rank reads its tokens' rows from the owners (peer loads); the step is one
+    CUDA graph (NCCL calls included). Strong scaling: the same tokens and table at every N."""
     from table_moe.cache_engine.sharded import ShardedCentroidTable, shard_range
 
     c = C5
     k0, k1 = shard_range(c["k"], world, rank)
     g = torch.Generator(device=device).manual_seed(5005)  # identical on every rank
     keys_full = torch.randn(1, 2, c["k"], c["l"], generator=g, device=device)
-    keys = keys_full[:, :, k0:k1].contiguous()
     proj = [orthonormal_basis(c["h"], c["l"], g, device) for _ in range(2)]
     pca = {m: {"proj": proj[i], "bias": torch.zeros(c["l"], device=device)} for i, m in enumerate(("vision", "text"))}
     x = torch.randn(c["tokens"], c["h"], generator=g, device=device).to(torch.bfloat16)
     vis = torch.zeros(c["tokens"], dtype=torch.bool, device=device)
     gv = torch.Generator(device=device).manual_seed(6006 + rank)
     values = torch.randn(1, 2, k1 - k0, c["h"], generator=gv, device=device, dtype=torch.bfloat16).mul_(0.05)
-    table = ShardedCentroidTable(keys, values, pca, c["k"])
+    table = ShardedCentroidTable(keys_full, values, pca, c["k"], replicate_keys=True)
     graph, (hit, idx, rows) = table.capture(x, vis)  # the whole lookup, NCCL calls included
 
     barrier(world)
@@ -640,8 +640,8 @@ def c5_workload(args, rank, world, device, flush, peaks, checker):
     t = total_ms / args.wl_steps / 1e3
     achieved = flops / t / 1e12
     return {
-        "config": "BASELINE config 5: one table K=65536, L=128 fp32, 65536x4096 bf16 rows, 32768 tokens "
-                  "(hidden 4096), centroid-range shards over the ranks",
+        "config": "BASELINE config 5: one table K=65536, L=128 fp32 (replicated), 65536x4096 bf16 rows (sharded), 32768 tokens "
+                  "(hidden 4096), value rows sharded by centroid range over the ranks",
         "value": round(c["tokens"] / t, 1), "unit": "lookups/s",
         "ms_per_step": round(t * 1e3, 4), "steps": args.wl_steps, "scaling": "strong",
         "shards": world, "l2": "flushed between steps (256 MB write outside the timed span)",

@@ -25,6 +25,14 @@ store before their next launch (``PeerLeftError``). Either error marks the table
 ``capture()`` records one whole lookup (NCCL calls included) as a CUDA graph, so that the
 per-call host work - argument marshalling, launches, collective calls - is paid once.
 
+Replicated keys (``replicate_keys=True``): the key table is small next to the value rows
+(C5: 32 MiB of fp32 keys against 512 MiB of bf16 rows), so every rank may hold all of it
+and only the value rows are split by centroid range. A lookup then needs no query or
+candidate exchange before the scan: rank r projects and scans its own Q/W tokens over the
+whole table, the packed winners (8 bytes per token) are all-gathered and merged so that
+every rank holds the global (hit, idx), and step 3 is unchanged. The scan's work divides by
+W with no fixed part over all Q tokens (strong scaling).
+
 The reference is single-GPU; this is the centroid-range sharding the benchmark's large-
 table configuration asks for. The device work goes through the C ABI; the three device
 steps are attributes of the object so that the exchange logic can be exercised on CPU
@@ -60,9 +68,10 @@ def shard_range(k_total: int, world: int, rank: int):
 class ShardedCentroidTable:
     def __init__(self, keys, values, pca, k_total, *, group=None, keyset=_alut.KEYS_RAW,
                  normalize=False, cmp_ge=False, thr_vision=0.0, thr_text=0.0, eps=1e-6, timeout_s=None,
-                 store=None):
-        """keys: [1, 2, Kr, L] this rank's slice (rows shard_range(k_total, W, r));
-        values: [1, 2, Kr, H]; pca: {"vision": {proj, bias}, "text": {...}}.
+                 store=None, replicate_keys=False):
+        """keys: [1, 2, Kr, L] this rank's slice (rows shard_range(k_total, W, r)), or with
+        replicate_keys the whole [1, 2, k_total, L] table on every rank;
+        values: [1, 2, Kr, H] this rank's slice; pca: {"vision": {proj, bias}, "text": {...}}.
         timeout_s: limit of every collective wait (None: the process group's own timeout);
         store: the store ``leave()`` announces through (default: the default group's)."""
         self.group = group
@@ -78,13 +87,19 @@ class ShardedCentroidTable:
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.k_total = int(k_total)
         self.k0, self.k1 = shard_range(self.k_total, self.world, self.rank)
-        if keys.shape[2] != self.k1 - self.k0:
-            raise ValueError(f"rank {self.rank} holds {keys.shape[2]} rows, expected {self.k1 - self.k0}")
+        self.replicate_keys = bool(replicate_keys)
+        want = self.k_total if self.replicate_keys else self.k1 - self.k0
+        if keys.shape[2] != want:
+            raise ValueError(f"rank {self.rank} holds {keys.shape[2]} key rows, expected {want}")
+        if values.shape[2] != self.k1 - self.k0:
+            raise ValueError(f"rank {self.rank} holds {values.shape[2]} value rows, expected {self.k1 - self.k0}")
+        self.key_base = 0 if self.replicate_keys else self.k0  # global index of this rank's first key row
         self.keys, self.values, self.pca = keys, values, pca
         self.device = keys.device
         self.params = dict(keyset=keyset, normalize=normalize, cmp_ge=cmp_ge, thr_vision=thr_vision,
                            thr_text=thr_text, eps=eps)
         self._tables = None
+        self._vtables = None
         self._ws = None
         self._peers = None  # (device pointers, shard starts, modality strides, opened mappings)
         # Device steps (replaceable for CPU tests of the exchange).
@@ -98,7 +113,8 @@ class ShardedCentroidTable:
             pv, pt = self.pca["vision"], self.pca["text"]
             k = self.keys if self.params["keyset"] == _alut.KEYS_NORMALISED else None
             r = self.keys if self.params["keyset"] == _alut.KEYS_RAW else None
-            self._tables = _alut.make_tables(k, r, self.values, pv["proj"], pv["bias"], pt["proj"], pt["bias"])
+            vals = None if self.replicate_keys else self.values  # replicated keys: K rows != value rows
+            self._tables = _alut.make_tables(k, r, vals, pv["proj"], pv["bias"], pt["proj"], pt["bias"])
             self._split = _alut.prepare_basis(self._tables, self.device)
             if self._split is not None:
                 self._tables.proj_split = self._split.data_ptr()
@@ -118,6 +134,19 @@ class ShardedCentroidTable:
                     else:
                         self._tables.keys_split = self._keys_split.data_ptr()
         return self._tables
+
+    def _value_tables(self):
+        """Tables whose values are this rank's slice (with replicated keys: the matching key
+        rows, so that the struct's K is the slice's)."""
+        if not self.replicate_keys:
+            return self._tables_struct()
+        if self._vtables is None:
+            pv, pt = self.pca["vision"], self.pca["text"]
+            ks = self.keys[:, :, self.k0:self.k1]
+            k = ks if self.params["keyset"] == _alut.KEYS_NORMALISED else None
+            r = ks if self.params["keyset"] == _alut.KEYS_RAW else None
+            self._vtables = _alut.make_tables(k, r, self.values, pv["proj"], pv["bias"], pt["proj"], pt["bias"])
+        return self._vtables
 
     def _params_struct(self):
         p = self.params
@@ -151,7 +180,7 @@ class ShardedCentroidTable:
         vis = is_vision.reshape(-1)
         packed = self._buf(q, "packed", (q,), torch.int64)
         b = _alut.make_batch(x, sel, vis, None)  # x, sel, vis stay referenced until the call returns
-        rc = lib.alut_search_packed(t, ctypes.byref(b), self._params_struct(), None, self.k0, packed.data_ptr(),
+        rc = lib.alut_search_packed(t, ctypes.byref(b), self._params_struct(), None, self.key_base, packed.data_ptr(),
                                     ws.data_ptr(), ws.numel(), _alut.stream_ptr(self.device))
         _alut.check(rc, "alut_search_packed")
         return packed
@@ -177,7 +206,7 @@ class ShardedCentroidTable:
         eids = torch.zeros(q, dtype=torch.int64, device=self.device)
         mids = torch.where(is_vision.reshape(-1).bool(), 0, 1).to(torch.int64).contiguous()
         out = torch.empty(q, self.values.shape[-1], dtype=self.values.dtype, device=self.device)
-        rc = lib.alut_gather_rows(self._tables_struct(), q, eids.data_ptr(), mids.data_ptr(), cids.data_ptr(), None,
+        rc = lib.alut_gather_rows(self._value_tables(), q, eids.data_ptr(), mids.data_ptr(), cids.data_ptr(), None,
                                   out.data_ptr(), out.stride(0), _alut.stream_ptr(self.device))
         _alut.check(rc, "alut_gather_rows")
         return out
@@ -252,7 +281,7 @@ class ShardedCentroidTable:
         b = _alut.make_batch(None, sel, vis, None)
         p = self.params
         prm = _alut.make_params(p["keyset"], False, p["cmp_ge"], p["thr_vision"], p["thr_text"], p["eps"])
-        rc = lib.alut_search_packed(t, ctypes.byref(b), prm, q_all.data_ptr(), self.k0, packed.data_ptr(),
+        rc = lib.alut_search_packed(t, ctypes.byref(b), prm, q_all.data_ptr(), self.key_base, packed.data_ptr(),
                                     ws.data_ptr(), ws.numel(), _alut.stream_ptr(self.device))
         _alut.check(rc, "alut_search_packed")
         return packed
@@ -332,7 +361,20 @@ class ShardedCentroidTable:
         is_vision = is_vision.reshape(-1)
         if is_vision.dtype != torch.bool or not is_vision.is_contiguous():
             is_vision = is_vision.bool().contiguous()
-        if self._nccl() and x.shape[0] % self.world == 0 and self.local_search == self._local_search:
+        q = x.shape[0]
+        if self.replicate_keys:
+            # Own tokens over the whole table, then the winners of every rank's tokens.
+            if q % self.world:
+                raise ValueError(f"token count {q} is not a multiple of the world size {self.world}")
+            lo, hi = q * self.rank // self.world, q * (self.rank + 1) // self.world
+            packed = self.local_search(x[lo:hi], is_vision[lo:hi])
+            if self.world > 1:
+                flat = self._buf(q, "flat", (q,), packed.dtype) if packed.device == self.device else \
+                    torch.empty(q, dtype=packed.dtype, device=packed.device)
+                self._all_gather(flat, packed.contiguous())
+                packed = flat
+            return self.merge(packed.view(1, -1), is_vision)
+        if self._nccl() and q % self.world == 0 and self.local_search == self._local_search:
             packed = self._local_search_q(self._project_split(x, is_vision), is_vision)
         else:
             packed = self.local_search(x, is_vision)

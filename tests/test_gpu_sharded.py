@@ -38,14 +38,15 @@ def _reference(device):
     return hit[:, 0].cpu(), idx[:, 0].cpu(), values
 
 
-def _sharded(device, world, rank):
+def _sharded(device, world, rank, replicate=False):
     from table_moe.cache_engine.sharded import ShardedCentroidTable, shard_range
 
     keys, values, proj, x, vis = _tables(device)
     k0, k1 = shard_range(K, world, rank)
     pca = {m: {"proj": proj[i].to(device), "bias": torch.zeros(L, device=device)} for i, m in enumerate(("vision", "text"))}
-    t = ShardedCentroidTable(keys[:, :, k0:k1].contiguous().to(device), values[:, :, k0:k1].contiguous().to(device),
-                             pca, K)
+    kr = keys if replicate else keys[:, :, k0:k1]
+    t = ShardedCentroidTable(kr.contiguous().to(device), values[:, :, k0:k1].contiguous().to(device),
+                             pca, K, replicate_keys=replicate)
     xd, vd = x.to(device), vis.to(device)
     hit, idx, rows = t.lookup(xd, vd)
     torch.cuda.synchronize(device)
@@ -60,14 +61,15 @@ def _check(hit, idx, rows, ref_hit, ref_idx, values, vis, lo, hi):
     assert torch.equal(rows.view(torch.int16), ref_rows[lo:hi].view(torch.int16))
 
 
-def test_sharded_world1_matches_search():
+@pytest.mark.parametrize("replicate", [False, True])
+def test_sharded_world1_matches_search(replicate):
     dev = torch.device("cuda:0")
     ref_hit, ref_idx, values = _reference(dev)
-    hit, idx, rows = _sharded(dev, 1, 0)
+    hit, idx, rows = _sharded(dev, 1, 0, replicate)
     _check(hit, idx, rows, ref_hit, ref_idx, values, _tables(dev)[4], 0, Q)
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, replicate):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -79,19 +81,20 @@ def _worker(rank, world, port, out):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
     try:
-        out[rank] = _sharded(dev, world, rank)
+        out[rank] = _sharded(dev, world, rank, replicate)
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sharded_world2_nccl_matches_search():
+@pytest.mark.parametrize("replicate", [False, True])
+def test_sharded_world2_nccl_matches_search(replicate):
     world = 2
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     out = mp.get_context("spawn").Manager().dict()
-    mp.start_processes(_worker, args=(world, port, out), nprocs=world, start_method="spawn", join=True)
+    mp.start_processes(_worker, args=(world, port, out, replicate), nprocs=world, start_method="spawn", join=True)
     dev = torch.device("cuda:0")
     ref_hit, ref_idx, values = _reference(dev)
     vis = _tables(dev)[4]

@@ -43,7 +43,7 @@ def _problem(seed=0, Q=12, K=10, L=4, H=6):
     return q, keys, values, vis
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, replicate=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -51,14 +51,18 @@ def _worker(rank, world, port, out):
         q, keys, values, vis = _problem()
         K = keys.shape[0]
         k0, k1 = shard_range(K, world, rank)
-        shard_keys = torch.from_numpy(keys[k0:k1]).view(1, 1, k1 - k0, -1).expand(1, 2, -1, -1).contiguous()
+        kk = keys if replicate else keys[k0:k1]
+        shard_keys = torch.from_numpy(kk).view(1, 1, len(kk), -1).expand(1, 2, -1, -1).contiguous()
         shard_vals = torch.from_numpy(values[k0:k1]).view(1, 1, k1 - k0, -1).expand(1, 2, -1, -1).contiguous()
-        t = ShardedCentroidTable(shard_keys, shard_vals, pca={}, k_total=K, thr_vision=-1e9, thr_text=0.5)
+        t = ShardedCentroidTable(shard_keys, shard_vals, pca={}, k_total=K, thr_vision=-1e9, thr_text=0.5,
+                                 replicate_keys=replicate)
+        seen = []
 
         def local_search(x, is_vision):
-            s = x.numpy() @ shard_keys[0, 0].numpy().T  # [Q, Kr]
+            seen.append(len(x))
+            s = x.numpy() @ shard_keys[0, 0].numpy().T  # [Q or Q/W, Kr]
             i = s.argmax(axis=1)
-            return torch.from_numpy(_pack(s[np.arange(len(i)), i], i + t.k0))
+            return torch.from_numpy(_pack(s[np.arange(len(i)), i], i + t.key_base))
 
         def merge(packed_all, is_vision):
             best = packed_all.numpy().view(np.uint64).max(axis=0)
@@ -75,7 +79,7 @@ def _worker(rank, world, port, out):
 
         t.local_search, t.merge, t.gather_owned = local_search, merge, gather_owned
         hit, idx, rows = t.lookup(torch.from_numpy(q), torch.from_numpy(vis))
-        out[rank] = (hit.numpy().copy(), idx.numpy().copy(), rows.numpy().copy())
+        out[rank] = (hit.numpy().copy(), idx.numpy().copy(), rows.numpy().copy(), seen)
     finally:
         dist.destroy_process_group()
 
@@ -86,11 +90,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_sharded_lookup_matches_unsharded():
+@pytest.mark.parametrize("replicate", [False, True])
+def test_sharded_lookup_matches_unsharded(replicate):
+    """Centroid-range keys (every rank scans its key slice for all tokens) and replicated keys
+    (every rank scans the whole table for its own tokens) give the same lookup."""
     world = 2
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
-    mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, start_method="spawn", join=True)
+    mp.start_processes(_worker, args=(world, _free_port(), out, replicate), nprocs=world, start_method="spawn",
+                       join=True)
     q, keys, values, vis = _problem()
     s = q @ keys.T
     idx = s.argmax(axis=1)  # first maximal index
@@ -99,7 +107,8 @@ def test_sharded_lookup_matches_unsharded():
     assert idx[3] == 2  # the planted tie resolves to the lower index
     Q = q.shape[0]
     for r in range(world):
-        h, i, rows = out[r]
+        h, i, rows, seen = out[r]
+        assert seen == [Q // world if replicate else Q]  # tokens each rank scanned
         assert np.array_equal(h, hit) and np.array_equal(i, np.where(hit, idx, 0))
         lo, hi = Q * r // world, Q * (r + 1) // world
         ref = np.where(hit[:, None], values[idx], 0.0)[lo:hi]
