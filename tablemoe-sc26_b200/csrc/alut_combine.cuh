@@ -75,6 +75,8 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
   ALUT_TRACE(21);
   pdl_wait();
   ALUT_TRACE(22);
+  bool my_surv = false, my_look = false;  // this thread's slot (a.s <= kCombineThreads)
+  const TV* my_off = nullptr;
   for (int s = tid; s < a.s; s += kCombineThreads) {
     const bool r = r_;
     const int64_t e = e_;
@@ -100,30 +102,56 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
     const bool comp = comp_;
     const bool look = hit && ev && idx >= 0 && idx < a.k;
     const bool add_comp = comp && !look && a.computed != nullptr;  // a hit row wins (cached_layers.py:452)
+    my_surv = comp || hit;
+    my_look = look || add_comp;
+    my_off = add_comp ? static_cast<const TV*>(a.computed) + t * a.computed_stride_t + s * a.computed_stride_s
+                      : static_cast<const TV*>(a.values) + (look ? (e * a.vs_e + m * a.vs_m + idx * a.vs_k) : 0);
     s_w[s] = w_;
-    s_surv[s] = (comp || hit) ? 1 : 0;
-    s_look[s] = (look || add_comp) ? 1 : 0;
-    s_off[s] = add_comp ? static_cast<const TV*>(a.computed) + t * a.computed_stride_t + s * a.computed_stride_s
-                        : static_cast<const TV*>(a.values) + (look ? (e * a.vs_e + m * a.vs_m + idx * a.vs_k) : 0);
+    s_surv[s] = my_surv ? 1 : 0;
+    s_look[s] = my_look ? 1 : 0;
+    s_off[s] = my_off;
   }
-  __syncthreads();
-  if (tid == 0) {
-    float kept = 0.f, tot = 0.f;
-    for (int s = 0; s < a.s; ++s) {
-      kept += s_surv[s] ? s_w[s] : 0.f;
-      tot += s_w[s];
+  if (a.s <= 32) {
+    // One warp: survivor and row sums by shuffles, the looked-up slots compacted in slot
+    // order by a ballot prefix (the accumulation below keeps slot order).
+    if (tid < 32) {
+      float kept = my_surv ? w_ : 0.f, tot = w_;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        kept += __shfl_xor_sync(0xffffffffu, kept, o);
+        tot += __shfl_xor_sync(0xffffffffu, tot, o);
+      }
+      const unsigned lm = __ballot_sync(0xffffffffu, my_look);
+      if (my_look) {
+        float w = w_;
+        if (a.renorm == ALUT_RENORM_TO_ONE) w = kept > 0.f ? w / kept : 0.f;
+        else if (a.renorm == ALUT_RENORM_TO_ROWSUM) w = kept > 0.f ? (w / kept) * tot : 0.f;
+        const int pos = __popc(lm & ((1u << tid) - 1u));
+        s_wl[pos] = w;
+        s_offl[pos] = my_off;
+      }
+      if (tid == 0) s_n = __popc(lm);
     }
-    int n = 0;
-    for (int s = 0; s < a.s; ++s) {
-      if (!s_look[s]) continue;
-      float w = s_w[s];
-      if (a.renorm == ALUT_RENORM_TO_ONE) w = kept > 0.f ? w / kept : 0.f;
-      else if (a.renorm == ALUT_RENORM_TO_ROWSUM) w = kept > 0.f ? (w / kept) * tot : 0.f;
-      s_wl[n] = w;
-      s_offl[n] = s_off[s];
-      ++n;
+  } else {
+    __syncthreads();
+    if (tid == 0) {
+      float kept = 0.f, tot = 0.f;
+      for (int s = 0; s < a.s; ++s) {
+        kept += s_surv[s] ? s_w[s] : 0.f;
+        tot += s_w[s];
+      }
+      int n = 0;
+      for (int s = 0; s < a.s; ++s) {
+        if (!s_look[s]) continue;
+        float w = s_w[s];
+        if (a.renorm == ALUT_RENORM_TO_ONE) w = kept > 0.f ? w / kept : 0.f;
+        else if (a.renorm == ALUT_RENORM_TO_ROWSUM) w = kept > 0.f ? (w / kept) * tot : 0.f;
+        s_wl[n] = w;
+        s_offl[n] = s_off[s];
+        ++n;
+      }
+      s_n = n;
     }
-    s_n = n;
   }
   __syncthreads();
   ALUT_TRACE(23);
