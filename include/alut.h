@@ -40,7 +40,7 @@
  *   alut_merge_packed     centroid-range sharding of one large table (new: the reference
  *                         is single-GPU; the merge rule is the tie rule of search.py:89)
  *
- * Input ordering: batches of <= 32 tokens (the decode chain) read sel, reuse and is_vision
+ * Input ordering: batches of <= 256 slots (q x s; the decode chain) read sel, reuse and is_vision
  * before waiting for the kernel that precedes the call on the stream, so that key copies
  * start early; these inputs must be complete when the call is issued (true for inputs
  * written by ordinary stream-ordered work). x is read only after that wait.
@@ -151,7 +151,7 @@ typedef struct alut_search_params {
 size_t alut_workspace_size(const alut_tables_t* tables, int32_t q, int32_t s);
 
 /* Which centroid scan a batch of q tokens x s slots takes on these tables (contiguous,
- * 16-byte aligned key rows assumed): the decode chain (<= 32 tokens and <= 256 slots),
+ * 16-byte aligned key rows assumed): the decode chain (<= 256 slots, any q),
  * the tensor-core scan (fp32 keys with L % 16 == 0, L <= 128, >= 512 slots and >= 12
  * slots per routed table on average; it needs the key form of alut_prepare_keys) or the
  * CUDA-core scans. Negative status on invalid arguments. */

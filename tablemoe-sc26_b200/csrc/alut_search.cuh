@@ -33,7 +33,12 @@ constexpr int kTmaBuffers = 2;
 constexpr uint32_t kWaitLimit = 1u << 20;  // bounded mbarrier wait (iterations of try_wait)
 constexpr int kBatch = 4;                   // slots scored together per pass over a row
 constexpr int kDecodeMaxPairs = 256;
-constexpr int kDecodeMaxTokens = 32;
+constexpr int kDecodeMaxTokens = kDecodeMaxPairs;  // any batch of <= 256 slots
+#ifndef ALUT_DECODE_RUN
+#define ALUT_DECODE_RUN 8
+#endif
+constexpr int kDecodeRun = ALUT_DECODE_RUN;  // slots of one table a decode-scan leader serves
+static_assert(kDecodeRun <= kSearchGroup, "runs fit the scoring group");
 
 // ---- TMA / mbarrier primitives ---------------------------------------------------------
 
@@ -429,22 +434,27 @@ __global__ void __launch_bounds__(kSearchThreads, LC == 128 ? 3 : 4) k_search_de
   __syncthreads();
   const int table = s_table[p];
   if (table < 0) return;
-  // Leader: the first searched slot routed to this table scans it for all of them.
-  int dup = 0;
-  for (int i = tid; i < p; i += kSearchThreads) dup |= (s_table[i] == table);
-  if (__syncthreads_or(dup)) return;
+  // Leaders: the searched slots routed to this table, in slot order, are served in runs of
+  // kDecodeRun; the first slot of each run scans the chunk for its run.
+  int before = 0;
+#pragma unroll
+  for (int i0 = 0; i0 < kDecodeMaxPairs; i0 += kSearchThreads) {
+    const int i = i0 + tid;
+    before += __syncthreads_count(i < p && s_table[i] == table);
+  }
+  if (before % kDecodeRun) return;
   if (warp == 0) {
     int n = 0;
-    for (int base = p; base < pairs && n < kSearchGroup; base += 32) {
+    for (int base = p; base < pairs && n < kDecodeRun; base += 32) {
       const int i = base + lane;
       const bool m = i < pairs && s_table[i] == table;
       const unsigned bal = __ballot_sync(0xffffffffu, m);
       const int pos = n + __popc(bal & ((1u << lane) - 1u));
-      if (m && pos < kSearchGroup) pid[pos] = i;
+      if (m && pos < kDecodeRun) pid[pos] = i;
       n += __popc(bal);
     }
     if (lane == 0) {
-      s_cnt = min(n, kSearchGroup);
+      s_cnt = min(n, kDecodeRun);
       s_abort = 0;
     }
   }

@@ -118,11 +118,13 @@ def test_integration_stub_matches_the_binding(stub, ours):
 
 
 def test_scan_kind_follows_the_measured_crossovers():
-    """alut_scan_kind is a host-side rule (no GPU): decode chain up to 32 tokens / 256 slots,
+    """alut_scan_kind is a host-side rule (no GPU): decode chain up to 256 slots,
     tensor-core scan from 512 slots with >= 12 slots per routed table, else CUDA-core."""
     lib = _alut.load()
     t, _ = _tables(E=128, K=1024, L=64, H=256)
     assert lib.alut_scan_kind(t, 16, 8) == _alut.SCAN_DECODE
+    assert lib.alut_scan_kind(t, 256, 1) == _alut.SCAN_DECODE        # any token count up to 256 slots
+    assert lib.alut_scan_kind(t, 33, 8) == _alut.SCAN_CUDA_CORE      # 264 slots
     assert lib.alut_scan_kind(t, 64, 8) == _alut.SCAN_CUDA_CORE      # 2 slots per table
     assert lib.alut_scan_kind(t, 512, 8) == _alut.SCAN_TENSOR_CORE   # 16 per table
     assert lib.alut_scan_kind(t, 4096, 8) == _alut.SCAN_TENSOR_CORE

@@ -200,6 +200,20 @@ def test_benchmark_shapes_match_oracle(cfg):
     check_combined(out.float().cpu().numpy(), ref, what=name)
 
 
+@pytest.mark.parametrize("Q,S,E,dtype", [(100, 2, 3, torch.bfloat16), (128, 2, 2, torch.float32),
+                                          (250, 1, 1, torch.bfloat16), (40, 6, 8, torch.float32)])
+def test_decode_chain_runs_of_slots_per_table(Q, S, E, dtype):
+    """Batches of <= 256 slots take the decode chain at any token count: a table with more
+    than 32 searched slots is scanned by one leader CTA per run of 32 of them."""
+    s = synth(Q=Q, S=S, E=E, K=300, L=64, H=512, seed=Q * 7 + E, vis_frac=0.3, reuse_p=0.9)
+    mgr = synth_manager(s)
+    assert _alut.load().alut_scan_kind(mgr.alut_tables(), Q, S) == _alut.SCAN_DECODE
+    hit, idx = gpu_dot(mgr, s, dtype=dtype)
+    q, keys, rh, ri = oracle_dot(s)
+    check_search(hit.cpu().numpy(), idx.cpu().numpy(), rh, ri, q, keys, s["sel"].numpy(), s["vis"].numpy(),
+                 (0.0, 0.0), "float32", what=f"decode runs Q{Q} S{S} E{E}")
+
+
 def test_projection_matches_oracle():
     s = synth(Q=300, S=2, E=2, K=8, L=96, H=1000, seed=3)
     mgr = synth_manager(s)
