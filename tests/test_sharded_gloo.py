@@ -123,7 +123,7 @@ def test_shard_ranges_cover_the_table():
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
 
 
-def _failing_worker(rank, world, port, scenario, out):
+def _failing_worker(rank, world, port, scenario, out, replicate=False):
     """Rank 1 stops after one lookup; rank 0's next lookup must end with an error within the
     limit instead of waiting: 'leave' announces it through the store, 'silent' just stops
     (rank 0's collective times out)."""
@@ -138,9 +138,10 @@ def _failing_worker(rank, world, port, scenario, out):
     q, keys, values, vis = _problem()
     K = keys.shape[0]
     k0, k1 = shard_range(K, world, rank)
-    shard_keys = torch.from_numpy(keys[k0:k1]).view(1, 1, k1 - k0, -1).expand(1, 2, -1, -1).contiguous()
+    kk = keys if replicate else keys[k0:k1]
+    shard_keys = torch.from_numpy(kk).view(1, 1, len(kk), -1).expand(1, 2, -1, -1).contiguous()
     shard_vals = torch.from_numpy(values[k0:k1]).view(1, 1, k1 - k0, -1).expand(1, 2, -1, -1).contiguous()
-    t = ShardedCentroidTable(shard_keys, shard_vals, pca={}, k_total=K, timeout_s=2.0)
+    t = ShardedCentroidTable(shard_keys, shard_vals, pca={}, k_total=K, timeout_s=2.0, replicate_keys=replicate)
     t.local_search = lambda x, v: torch.from_numpy(_pack(np.zeros(len(x), np.float32), np.full(len(x), t.k0)))
     t.merge = lambda p, v: (torch.ones(p.shape[1], dtype=torch.bool), p[0] & 0)
     t.gather_owned = lambda h, i, v: torch.zeros(len(h), shard_vals.shape[-1])
@@ -170,11 +171,13 @@ def _failing_worker(rank, world, port, scenario, out):
 
 
 @pytest.mark.timeout(120)
-@pytest.mark.parametrize("scenario,expect,limit", [("leave", "left", 1.0), ("silent", "timeout", 10.0)])
-def test_sharded_lookup_fails_fast_when_a_rank_stops(scenario, expect, limit):
+@pytest.mark.parametrize("scenario,expect,limit,replicate", [("leave", "left", 1.0, False),
+                                                             ("silent", "timeout", 10.0, False),
+                                                             ("silent", "timeout", 10.0, True)])
+def test_sharded_lookup_fails_fast_when_a_rank_stops(scenario, expect, limit, replicate):
     world = 2
     out = mp.get_context("spawn").Manager().dict()
-    ctx = mp.start_processes(_failing_worker, args=(world, _free_port(), scenario, out), nprocs=world,
+    ctx = mp.start_processes(_failing_worker, args=(world, _free_port(), scenario, out, replicate), nprocs=world,
                              start_method="spawn", join=False)
     while not ctx.join(timeout=60):
         pass
