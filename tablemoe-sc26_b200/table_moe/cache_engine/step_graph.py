@@ -43,6 +43,11 @@ def _view(arena: torch.Tensor, off: int, shape, dtype):
 
 
 class LookupStepGraph:
+    # Copy plan of a captured step with copies: layers at which a new host->device input copy
+    # starts (besides 0), and the layer stride of the device->host output copies.
+    INPUT_CUTS = (2, 8)
+    OUTPUT_EVERY = 4
+
     def __init__(self, engines, q, s, *, x_dtype=torch.bfloat16, variant="decode", renorm="to_one",
                  accumulate=True, keep_hits=False):
         """``keep_hits``: every layer's lookup also writes its hits and centroid indices into
@@ -115,17 +120,18 @@ class LookupStepGraph:
                 b.out.copy_(out)
 
     def _step_with_copies(self, lib):
-        """Inputs in two copies (the first layers' alone, so that the first lookup starts
-        early; the rest while it runs), outputs every four layers and the last layer's alone
-        (so that little is left to copy after the last lookup), all on a second stream. The
-        lookups wait only at the two input boundaries, so programmatic launch still chains
-        the other layers."""
+        """Inputs in three copies of growing size (layers 0-1 alone, so that the first lookup
+        starts early; layers 2-7 while those run; the rest while layers 2-7 run, each copy
+        landing before its first layer is reached), outputs every four layers and the last
+        layer's alone (so that little is left to copy after the last lookup), all on a second
+        stream. The lookups wait only at the three input boundaries, so programmatic launch
+        still chains the other layers."""
         main = torch.cuda.current_stream(self.device)
         copy = torch.cuda.Stream(self.device)
         copy.wait_stream(main)
         n = len(self.engines)
-        in_cuts = sorted({0, min(2, n), n})
-        out_cuts = sorted(set(range(0, n, 4)) | {max(0, n - 1), n})
+        in_cuts = sorted({0, n} | {min(c, n) for c in self.INPUT_CUTS})
+        out_cuts = sorted(set(range(0, n, self.OUTPUT_EVERY)) | {max(0, n - 1), n})
         landed = {}
         with torch.cuda.stream(copy):
             for lo, hi in zip(in_cuts, in_cuts[1:]):
