@@ -225,7 +225,7 @@ def known_answer(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="checkout of the reference project")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from table_moe.cache_engine import manager as manager_mod
